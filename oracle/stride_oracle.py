@@ -1,0 +1,196 @@
+"""Test infrastructure: a NumPy restatement of the reference's stride
+primitives, used only as the checker of the CUDA engine.
+
+Each function states the reference semantics it follows.  Address arithmetic
+is exact (integer index arrays); floating-point results are bit-identical to
+the reference's CPU executors for copies, real scalings and real sums whose
+contributions do not collide.  Complex scalings use NumPy's complex product
+(no fused multiply-add), so they match to rounding only.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def decode_layout(words):
+    """Records of v1 layout words (src/tensor0/_stride/_ffi/_descriptor.py:8-32)."""
+    w = [int(x) for x in np.asarray(words, dtype=np.int64)]
+    assert w[0] == 1, "unsupported layout version"
+    source_size, output_size, count = w[1], w[2], w[3]
+    records, at = [], 4
+    for _ in range(count):
+        rank, src_off, dst_off = w[at], w[at + 1], w[at + 2]
+        at += 3
+        shape = w[at:at + rank]; at += rank
+        sstr = w[at:at + rank]; at += rank
+        dstr = w[at:at + rank]; at += rank
+        records.append((tuple(shape), tuple(sstr), src_off, tuple(dstr), dst_off))
+    return source_size, output_size, records
+
+
+def decode_reduction_layout(words):
+    """Records and reduction roles of reduction words (_descriptor.py:41-76)."""
+    w = np.asarray(words, dtype=np.int64).view(np.uint64)
+    w = [int(x) for x in w]
+
+    def signed(x):
+        return x - (1 << 64) if x >= 1 << 63 else x
+
+    assert w[0] == 1, "unsupported reduction layout version"
+    source_size, output_size, count = w[1], w[2], w[3]
+    records, at = [], 4
+    for _ in range(count):
+        rank, src_off, dst_off = w[at], w[at + 1], w[at + 2]
+        at += 3
+        shape = w[at:at + rank]; at += rank
+        sstr = [signed(x) for x in w[at:at + rank]]; at += rank
+        at += rank  # output shape (implied by roles)
+        dstr = [signed(x) for x in w[at:at + rank]]; at += rank
+        roles = [bool(x) for x in w[at:at + rank]]; at += rank
+        dstr = [0 if r else d for d, r in zip(dstr, roles)]
+        records.append((tuple(shape), tuple(sstr), src_off, tuple(dstr), dst_off, tuple(roles)))
+    return source_size, output_size, records
+
+
+def addresses(shape, strides, offset) -> np.ndarray:
+    """Flat addresses of a strided box in C order of its logical index."""
+    index = np.full(tuple(shape), offset, dtype=np.int64)
+    for axis, (size, stride) in enumerate(zip(shape, strides)):
+        view = (1,) * axis + (size,) + (1,) * (len(shape) - axis - 1)
+        index = index + np.arange(size, dtype=np.int64).reshape(view) * stride
+    return index.reshape(-1)
+
+
+def _zero_plus(values: np.ndarray) -> np.ndarray:
+    """0 + x, elementwise (turns -0 into +0)."""
+    return np.zeros_like(values) + values
+
+
+def copy(words, source: np.ndarray) -> np.ndarray:
+    """Copy: zero output, then out[dst] = src[src] bit for bit
+    (crates/tensor0-py/native/execute/copy.h:28-46, 119-134)."""
+    _, output_size, records = decode_layout(words)
+    view = source.view(np.uint8).reshape(*source.shape[:-1], source.shape[-1], source.itemsize)
+    out = np.zeros((*source.shape[:-1], output_size, source.itemsize), np.uint8)
+    for shape, sstr, so, dstr, do in records:
+        if int(np.prod(shape)) == 0:
+            continue
+        out[..., addresses(shape, dstr, do), :] = view[..., addresses(shape, sstr, so), :]
+    return out.reshape(*source.shape[:-1], output_size * source.itemsize).view(source.dtype)
+
+
+def _factor(coefficient, batch_shape):
+    c = np.asarray(coefficient)
+    if c.ndim == 0 or c.shape == (1,):
+        return c.reshape(()), True
+    return c.reshape(*batch_shape, 1), False
+
+
+def accumulation(words, source: np.ndarray, coefficients=(), coefficient_records=()) -> np.ndarray:
+    """Accumulation: out = 0; per record in order out[dst] += c * src[src];
+    a zero coefficient skips the record, a unit one the product
+    (ffi/reduction_impl.h:99-118; execute/reduction.h:18-94)."""
+    _, output_size, records = decode_layout(words)
+    factors = dict(zip((int(r) for r in coefficient_records), coefficients))
+    batch_shape = source.shape[:-1]
+    out = np.zeros((*batch_shape, output_size), source.dtype)
+    for index, (shape, sstr, so, dstr, do) in enumerate(records):
+        if int(np.prod(shape)) == 0:
+            continue
+        values = source[..., addresses(shape, sstr, so)]
+        if index in factors:
+            c, shared = _factor(factors[index], batch_shape)
+            if shared and c == 0:
+                continue
+            if not (shared and c == 1):
+                values = _scale(c, values, source.dtype)
+                if not shared:
+                    values = np.where(c == 0, np.zeros_like(values), values)
+        dst = addresses(shape, dstr, do)
+        _scatter_add(out, dst, values)
+    return out
+
+
+def _scale(c, values, dtype):
+    c = np.asarray(c)
+    if np.iscomplexobj(values) and not np.iscomplexobj(c):
+        real = values.real.dtype
+        c = c.astype(real)
+        return (c * values.real + 1j * (c * values.imag)).astype(dtype)
+    return (c.astype(dtype) * values).astype(dtype)
+
+
+def _scatter_add(out, dst, values):
+    """out[..., dst] += values, summing repeated destinations in order."""
+    unique = np.unique(dst).size == dst.size
+    if unique:
+        out[..., dst] = out[..., dst] + values
+    else:
+        flat = out.reshape(-1, out.shape[-1])
+        vals = values.reshape(-1, values.shape[-1])
+        for b in range(flat.shape[0]):
+            np.add.at(flat[b], dst, vals[b])
+
+
+def update(words, source: np.ndarray, base: np.ndarray, alpha, beta) -> np.ndarray:
+    """Update: out = base; out[dst] = a*src + b*base[dst] with zero/one
+    short-circuits (execute/update.h:28-77; map_reduce_policies.cuh:30-69)."""
+    _, _, records = decode_layout(words)
+    out = base.copy()
+    batch_shape = base.shape[:-1]
+    a, _ = _factor(alpha, batch_shape)
+    b, _ = _factor(beta, batch_shape)
+    for shape, sstr, so, dstr, do in records:
+        if int(np.prod(shape)) == 0:
+            continue
+        dst = addresses(shape, dstr, do)
+        s = source[..., addresses(shape, sstr, so)]
+        o = base[..., dst]
+        a0, a1 = np.all(a == 0), np.all(a == 1)
+        b0, b1 = np.all(b == 0), np.all(b == 1)
+        if a0:
+            value = np.zeros_like(o) if b0 else (o if b1 else _scale(b, o, base.dtype))
+        else:
+            st = s if a1 else _scale(a, s, base.dtype)
+            value = st if b0 else (st + (o if b1 else _scale(b, o, base.dtype))).astype(base.dtype)
+        out[..., dst] = value
+    return out
+
+
+def reduction(words, source: np.ndarray, coefficients=(), coefficient_records=()) -> np.ndarray:
+    """Reduction (partial trace): out = 0; per record out[owner] +=
+    c * sum over reduction axes (ffi/reduction_impl.h:29-150)."""
+    _, output_size, records = decode_reduction_layout(words)
+    factors = dict(zip((int(r) for r in coefficient_records), coefficients))
+    batch_shape = source.shape[:-1]
+    out = np.zeros((*batch_shape, output_size), source.dtype)
+    for index, (shape, sstr, so, dstr, do, roles) in enumerate(records):
+        if int(np.prod(shape)) == 0:
+            continue
+        values = source[..., addresses(shape, sstr, so)]
+        if index in factors:
+            c, shared = _factor(factors[index], batch_shape)
+            if shared and c == 0:
+                continue
+            if not (shared and c == 1):
+                values = _scale(c, values, source.dtype)
+        _scatter_add(out, addresses(shape, dstr, do), values)
+    return out
+
+
+def sector_gemm(spec, left: np.ndarray, right: np.ndarray, output_size: int) -> np.ndarray:
+    """C_g = A_g @ B_g per sector row {m, n, k, a_off, b_off, c_off}, computed
+    in float64 / complex128 (stand-in for the XLA dot of linalg.py:560)."""
+    wide = np.complex128 if np.iscomplexobj(left) else np.float64
+    out = np.zeros(output_size, wide)
+    for m, n, k, a, b, c in np.asarray(spec, np.int64).reshape(-1, 6):
+        if m * n == 0:
+            continue
+        if k == 0:
+            out[c:c + m * n] = 0
+            continue
+        A = left[a:a + m * k].reshape(m, k).astype(wide)
+        B = right[b:b + k * n].reshape(k, n).astype(wide)
+        out[c:c + m * n] = (A @ B).reshape(-1)
+    return out

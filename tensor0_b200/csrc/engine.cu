@@ -1,0 +1,493 @@
+// Map and reduce engines: the grouped strided permute / accumulate / update
+// kernel and the two-pass segmented reduction for partial traces.
+//
+// The map kernel is one persistent grid over every tile of every record of
+// every batch.  A tile is a box over the record's destination-innermost axis
+// X, its source-innermost axis Y and one further axis Z; it is read with lanes
+// running along Y (coalesced source reads), staged in shared memory and
+// written with lanes running along X (coalesced destination writes).  When X
+// and Y coincide the tile is copied row by row without staging.
+#include "engine.h"
+
+#include "arith.cuh"
+
+#include <algorithm>
+#include <atomic>
+
+namespace t0b {
+
+std::atomic<uint64_t> g_kernel_launches{0};
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// Division by a runtime divisor below 2^24 for dividends below 2^24.
+struct FastDiv {
+  uint32_t d, m, l;
+  __device__ __forceinline__ explicit FastDiv(uint32_t divisor) : d(divisor) {
+    l = 32 - __clz(divisor - 1);                         // ceil(log2(d)), d >= 1
+    const uint64_t one = 1;
+    m = static_cast<uint32_t>(((one << 32) * ((one << l) - divisor)) / divisor + 1);
+  }
+  __device__ __forceinline__ uint32_t Div(uint32_t n) const {
+    return (__umulhi(n, m) + n) >> l;
+  }
+};
+
+// Load one MapRecord field set into registers.
+struct TileView {
+  int64_t so, dof;           // source / destination element offsets of the tile origin
+  int64_t sx, sy, sz, dx, dy, dz;
+  int ex, ey, ez;            // actual tile extents
+  int px, ty;                // shared-memory pitch along X and tile extent along Y
+  int mode;
+  int slot;
+};
+
+__device__ __forceinline__ int64_t FindRecord(const MapRecord* recs, int64_t count, int64_t local) {
+  int64_t lo = 0, hi = count - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ TileView DecodeTile(const MapRecord& r, int64_t local, int64_t batch,
+                                               int64_t src_size, int64_t out_size) {
+  TileView v;
+  int64_t q = local - r.tile_begin;
+  const int c0 = r.c[0], c1 = r.c[1], c2 = r.c[2];
+  const int cx = static_cast<int>(q % c0); q /= c0;
+  const int cy = static_cast<int>(q % c1); q /= c1;
+  const int cz = static_cast<int>(q % c2); q /= c2;
+  v.so = r.src_off + batch * src_size;
+  v.dof = r.dst_off + batch * out_size;
+  for (int i = 0; i < r.nouter; ++i) {
+    const int64_t n = r.n[3 + i];
+    const int64_t idx = q % n;
+    q /= n;
+    v.so += idx * r.s[3 + i];
+    v.dof += idx * r.d[3 + i];
+  }
+  const int x0 = cx * r.t[0], y0 = cy * r.t[1], z0 = cz * r.t[2];
+  v.ex = min(r.t[0], r.n[0] - x0);
+  v.ey = min(r.t[1], r.n[1] - y0);
+  v.ez = min(r.t[2], r.n[2] - z0);
+  v.sx = r.s[0]; v.sy = r.s[1]; v.sz = r.s[2];
+  v.dx = r.d[0]; v.dy = r.d[1]; v.dz = r.d[2];
+  v.so += x0 * v.sx + y0 * v.sy + z0 * v.sz;
+  v.dof += x0 * v.dx + y0 * v.dy + z0 * v.dz;
+  v.px = r.t[0] | 1;         // odd pitch: conflict-free column writes
+  v.ty = r.t[1];
+  v.mode = r.mode;
+  v.slot = r.coef_slot;
+  return v;
+}
+
+// Walk `rows` rows of `len` elements: whole warps per row for long rows,
+// several rows per warp for short ones.  f(row, col).
+template <typename F>
+__device__ __forceinline__ void ForRows(int rows, int len, F&& f) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (len > 16) {
+    for (int r = warp; r < rows; r += kWarps) {
+#pragma unroll 2
+      for (int c = lane; c < len; c += 32) f(r, c);
+    }
+  } else {
+    const int per = 32 / len;
+    const int sub = lane / len;
+    const int col = lane - sub * len;
+    if (sub >= per) return;
+#pragma unroll 4
+    for (int r = warp * per + sub; r < rows; r += kWarps * per) f(r, col);
+  }
+}
+
+// Per-operation element function applied when a value reaches the destination.
+template <int Op, typename T, typename CA, typename CB>
+struct Emit;
+
+// Copy: bit-preserving move (T is an unsigned storage type).
+template <typename T, typename CA, typename CB>
+struct Emit<kOpCopy, T, CA, CB> {
+  __device__ __forceinline__ Emit(const MapArgs&, int, int64_t) {}
+  __device__ __forceinline__ bool SkipSource() const { return false; }
+  __device__ __forceinline__ T operator()(T v, const T*, int64_t) const { return v; }
+};
+
+// Accumulation into a zeroed output: 0 + c * v, with the zero/one rules.
+template <typename T, typename CA, typename CB>
+struct Emit<kOpAccumulation, T, CA, CB> {
+  using Real = typename Elem<T>::Real;
+  using C = typename BoundOf<Real, CA>::type;
+  C c;
+  bool zero, one;
+  __device__ __forceinline__ Emit(const MapArgs& a, int slot, int64_t batch) {
+    if (slot < 0) {
+      zero = false; one = true; c = C{};
+    } else {
+      c = ReadCoefficient<Real>(static_cast<const CA*>(a.ca), slot, a.ca_count, batch);
+      zero = IsZero(c); one = IsOne(c);
+    }
+  }
+  __device__ __forceinline__ bool SkipSource() const { return zero; }
+  __device__ __forceinline__ T operator()(T v, const T*, int64_t) const {
+    if (zero) return Zero<T>();
+    return PlusZero(one ? v : Scale(c, v));
+  }
+};
+
+// Update: alpha * src + beta * base with the reference's short-circuits.
+template <typename T, typename CA, typename CB>
+struct Emit<kOpUpdate, T, CA, CB> {
+  using Real = typename Elem<T>::Real;
+  using A = typename BoundOf<Real, CA>::type;
+  using B = typename BoundOf<Real, CB>::type;
+  A a; B b;
+  bool a0, a1, b0, b1;
+  __device__ __forceinline__ Emit(const MapArgs& args, int, int64_t batch) {
+    a = ReadCoefficient<Real>(static_cast<const CA*>(args.ca), 0, args.ca_count, batch);
+    b = ReadCoefficient<Real>(static_cast<const CB*>(args.cb), 0, args.cb_count, batch);
+    a0 = IsZero(a); a1 = IsOne(a); b0 = IsZero(b); b1 = IsOne(b);
+  }
+  __device__ __forceinline__ bool SkipSource() const { return a0; }
+  __device__ __forceinline__ T operator()(T v, const T* base, int64_t at) const {
+    if (a0) {
+      if (b0) return Zero<T>();
+      const T old = base[at];
+      return b1 ? old : Scale(b, old);
+    }
+    const T s = a1 ? v : Scale(a, v);
+    if (b0) return s;
+    const T old = base[at];
+    return Add(s, b1 ? old : Scale(b, old));
+  }
+};
+
+template <int Op, typename T, typename CA, typename CB>
+__global__ void __launch_bounds__(kThreads) MapKernel(MapArgs args) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* tile = reinterpret_cast<T*>(smem_raw);
+  const T* __restrict__ src = static_cast<const T*>(args.src);
+  const T* base = static_cast<const T*>(args.base);
+  T* out = static_cast<T*>(args.out);
+  const int64_t total = args.tiles_per_batch * args.batches;
+  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+    const int64_t batch = t / args.tiles_per_batch;
+    const int64_t local = t - batch * args.tiles_per_batch;
+    const MapRecord& rec = args.recs[FindRecord(args.recs, args.nrec, local)];
+    const TileView v = DecodeTile(rec, local, batch, args.src_size, args.out_size);
+    const Emit<Op, T, CA, CB> emit(args, v.slot, batch);
+    const bool skip = emit.SkipSource();
+    if (v.mode == kDirect || skip) {
+      // Rows along X; with a skipped source only the destination side is touched.
+      const int rows = v.ey * v.ez;
+      ForRows(rows, v.ex, [&](int r, int x) {
+        const int z = r / v.ey;
+        const int y = r - z * v.ey;
+        const int64_t at = v.dof + x * v.dx + y * v.dy + z * v.dz;
+        T value{};
+        if (!skip) value = src[v.so + x * v.sx + y * v.sy + z * v.sz];
+        out[at] = emit(value, base, at);
+      });
+    } else {
+      // Load: rows along Y, one per (x, z).
+      const FastDiv by_ex(static_cast<uint32_t>(v.ex));
+      ForRows(v.ex * v.ez, v.ey, [&](int r, int y) {
+        const int z = static_cast<int>(by_ex.Div(static_cast<uint32_t>(r)));
+        const int x = r - z * v.ex;
+        tile[x + v.px * (y + v.ty * z)] = src[v.so + x * v.sx + y * v.sy + z * v.sz];
+      });
+      __syncthreads();
+      // Store: rows along X, one per (y, z).
+      const FastDiv by_ey(static_cast<uint32_t>(v.ey));
+      ForRows(v.ey * v.ez, v.ex, [&](int r, int x) {
+        const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
+        const int y = r - z * v.ey;
+        const int64_t at = v.dof + x * v.dx + y * v.dy + z * v.dz;
+        out[at] = emit(tile[x + v.px * (y + v.ty * z)], base, at);
+      });
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Reduce engine.
+
+__device__ __forceinline__ int64_t FindGroup(const ReduceGroup* groups, int64_t lo, int64_t hi,
+                                             int64_t value, bool by_task) {
+  hi -= 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    const int64_t key = by_task ? groups[mid].task_begin : groups[mid].owner_begin;
+    if (key <= value) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+template <typename T>
+__device__ __forceinline__ T WarpSum(T v) {
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) {
+    if constexpr (Elem<T>::kComplex) {
+      T other;
+      other.x = __shfl_xor_sync(0xffffffffu, v.x, offset);
+      other.y = __shfl_xor_sync(0xffffffffu, v.y, offset);
+      v = Add(v, other);
+    } else {
+      v = Add(v, __shfl_xor_sync(0xffffffffu, v, offset));
+    }
+  }
+  return v;
+}
+
+// Pass 1: one warp per (owner, chunk of records); lanes stride the fibers.
+template <typename T, typename CA>
+__global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
+  using Real = typename Elem<T>::Real;
+  using C = typename BoundOf<Real, CA>::type;
+  const T* __restrict__ src = static_cast<const T*>(args.src);
+  T* scratch = static_cast<T*>(args.scratch);
+  const int lane = threadIdx.x & 31;
+  const int64_t wave_tasks = args.task_end - args.task_begin;
+  const int64_t total = wave_tasks * args.batches;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5; w < total;
+       w += (static_cast<int64_t>(gridDim.x) * kThreads) >> 5) {
+    const int64_t batch = w / wave_tasks;
+    const int64_t task = args.task_begin + (w - batch * wave_tasks);
+    const ReduceGroup& g = args.groups[FindGroup(args.groups, args.group_begin, args.group_end, task, true)];
+    const int64_t local = task - g.task_begin;
+    const int64_t chunk = local / g.owners;
+    const int64_t owner = local - chunk * g.owners;
+    // Owner coordinates (map axes, innermost first).
+    int idx[kMaxRank];
+    int64_t rem = owner;
+    for (int a = 0; a < g.rank; ++a) { idx[a] = static_cast<int>(rem % g.n[a]); rem /= g.n[a]; }
+    const int64_t first = g.rec_begin + chunk * g.chunk_records;
+    const int64_t last = min(g.rec_end, first + g.chunk_records);
+    T acc{};
+    for (int64_t r = first; r < last; ++r) {
+      const ReduceRecord& rec = args.records[r];
+      C c{};
+      bool one = true;
+      if (rec.coef_slot >= 0) {
+        c = ReadCoefficient<Real>(static_cast<const CA*>(args.ca), rec.coef_slot, args.ca_count, batch);
+        if (IsZero(c)) continue;
+        one = IsOne(c);
+      }
+      int64_t at = rec.src_off + batch * args.src_size;
+      for (int a = 0; a < rec.map_rank; ++a) at += idx[a] * rec.s[a];
+      const int fr = rec.fiber_rank, mr = rec.map_rank;
+      for (int f = lane; f < rec.fiber_count; f += 32) {
+        int64_t off = 0;
+        int rest = f;
+        for (int a = 0; a < fr; ++a) {
+          const int n = rec.n[mr + a];
+          const int i = rest % n;
+          rest /= n;
+          off += i * rec.s[mr + a];
+        }
+        const T value = src[at + off];
+        acc = Add(acc, one ? value : Scale(c, value));
+      }
+    }
+    acc = WarpSum(acc);
+    if (lane == 0) scratch[batch * args.scratch_stride + g.scratch_off + chunk * g.owners + owner] = acc;
+  }
+}
+
+// Pass 2: one thread per owner; chunks combined in record order.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ReduceFinish(ReduceArgs args) {
+  const T* scratch = static_cast<const T*>(args.scratch);
+  T* out = static_cast<T*>(args.out);
+  const int64_t wave_owners = args.owner_end - args.owner_begin;
+  const int64_t total = wave_owners * args.batches;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int64_t batch = i / wave_owners;
+    const int64_t owner_id = args.owner_begin + (i - batch * wave_owners);
+    const ReduceGroup& g = args.groups[FindGroup(args.groups, args.group_begin, args.group_end, owner_id, false)];
+    const int64_t owner = owner_id - g.owner_begin;
+    const T* partial = scratch + batch * args.scratch_stride + g.scratch_off + owner;
+    T sum = partial[0];
+    for (int k = 1; k < g.chunks; ++k) sum = Add(sum, partial[static_cast<int64_t>(k) * g.owners]);
+    int64_t at = g.dst_off + batch * args.out_size;
+    int64_t rem = owner;
+    for (int a = 0; a < g.rank; ++a) { at += (rem % g.n[a]) * g.d[a]; rem /= g.n[a]; }
+    out[at] = Add(out[at], sum);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// TensorMap.add.
+
+template <typename T, typename S>
+__global__ void __launch_bounds__(kThreads) AxpbyKernel(int64_t n, S alpha, const T* __restrict__ x,
+                                                      S beta, const T* __restrict__ y, T* out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kThreads) {
+    out[i] = Add(Scale(alpha, x[i]), Scale(beta, y[i]));
+  }
+}
+
+int SmCount() {
+  static int count = [] {
+    int device = 0, sms = 148;
+    if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms;
+  }();
+  return count;
+}
+
+template <int Op, typename T, typename CA, typename CB>
+void LaunchMapTyped(const MapArgs& args, int smem, cudaStream_t stream) {
+  auto kernel = MapKernel<Op, T, CA, CB>;
+  static bool configured = false;
+  if (!configured) {
+    Check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024), "map attribute");
+    configured = true;
+  }
+  const int64_t total = args.tiles_per_batch * args.batches;
+  int per_sm = 0;
+  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem), "map occupancy");
+  const int64_t grid = std::min<int64_t>(total, static_cast<int64_t>(std::max(per_sm, 1)) * SmCount());
+  kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+  Check(cudaGetLastError(), "map launch");
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+template <typename Real, typename Complex, typename F>
+void VisitCoefficient(int32_t dtype, bool complex_storage, F&& f) {
+  if (dtype == 4) { f(static_cast<const int32_t*>(nullptr)); return; }
+  if ((dtype == 11 && sizeof(Real) == 4) || (dtype == 12 && sizeof(Real) == 8)) {
+    f(static_cast<const Real*>(nullptr)); return;
+  }
+  if (complex_storage && ((dtype == 15 && sizeof(Real) == 4) || (dtype == 18 && sizeof(Real) == 8))) {
+    f(static_cast<const Complex*>(nullptr)); return;
+  }
+  throw InvalidArgumentError("unsupported CUDA coefficient dtype; expected S32 or matching real/complex precision");
+}
+
+template <typename T, typename F>
+void WithStorage(int32_t dtype, F&& f) {
+  switch (dtype) {
+    case 11: f(static_cast<float*>(nullptr)); return;
+    case 12: f(static_cast<double*>(nullptr)); return;
+    case 15: f(static_cast<float2*>(nullptr)); return;
+    case 18: f(static_cast<double2*>(nullptr)); return;
+    default: throw InvalidArgumentError("CUDA stride storage supports only F32/F64/C64/C128");
+  }
+}
+
+}  // namespace
+
+int MapSharedBytes(const MapRecord* recs, int64_t count, int element_bytes) {
+  int64_t best = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    if (recs[i].mode != kTranspose) continue;
+    best = std::max<int64_t>(best, int64_t{recs[i].t[0] | 1} * recs[i].t[1] * recs[i].t[2] * element_bytes);
+  }
+  return static_cast<int>(best);
+}
+
+void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
+               int smem, cudaStream_t stream) {
+  WithStorage<void>(dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    using Real = typename Elem<T>::Real;
+    using Complex = std::conditional_t<sizeof(Real) == 4, float2, double2>;
+    constexpr bool kComplex = Elem<T>::kComplex;
+    if (op == kOpCopy) {
+      using Bits = std::conditional_t<sizeof(T) == 4, uint32_t, std::conditional_t<sizeof(T) == 8, uint2, uint4>>;
+      LaunchMapTyped<kOpCopy, Bits, int32_t, int32_t>(args, smem, stream);
+    } else if (op == kOpAccumulation) {
+      VisitCoefficient<Real, Complex>(ca_dtype, kComplex, [&](auto* ca) {
+        using CA = std::remove_cv_t<std::remove_pointer_t<decltype(ca)>>;
+        if constexpr (!kComplex && sizeof(CA) == 2 * sizeof(Real)) {
+        } else {
+          LaunchMapTyped<kOpAccumulation, T, CA, int32_t>(args, smem, stream);
+        }
+      });
+    } else {
+      VisitCoefficient<Real, Complex>(ca_dtype, kComplex, [&](auto* ca) {
+        using CA = std::remove_cv_t<std::remove_pointer_t<decltype(ca)>>;
+        VisitCoefficient<Real, Complex>(cb_dtype, kComplex, [&](auto* cb) {
+          using CB = std::remove_cv_t<std::remove_pointer_t<decltype(cb)>>;
+          if constexpr (!kComplex && (sizeof(CA) == 2 * sizeof(Real) || sizeof(CB) == 2 * sizeof(Real))) {
+          } else {
+            LaunchMapTyped<kOpUpdate, T, CA, CB>(args, smem, stream);
+          }
+        });
+      });
+    }
+  });
+}
+
+void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream) {
+  WithStorage<void>(dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    using Real = typename Elem<T>::Real;
+    using Complex = std::conditional_t<sizeof(Real) == 4, float2, double2>;
+    constexpr bool kComplex = Elem<T>::kComplex;
+    VisitCoefficient<Real, Complex>(ca_dtype, kComplex, [&](auto* ca) {
+      using CA = std::remove_cv_t<std::remove_pointer_t<decltype(ca)>>;
+      if constexpr (!kComplex && sizeof(CA) == 2 * sizeof(Real)) {
+      } else {
+        const int64_t warps = (args.task_end - args.task_begin) * args.batches;
+        if (warps > 0) {
+          const int64_t grid = std::min<int64_t>((warps + kWarps - 1) / kWarps, int64_t{SmCount()} * 16);
+          ReducePartials<T, CA><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(args);
+          Check(cudaGetLastError(), "reduce launch");
+          g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+        }
+        const int64_t threads = (args.owner_end - args.owner_begin) * args.batches;
+        if (threads > 0) {
+          const int64_t grid = std::min<int64_t>((threads + kThreads - 1) / kThreads, int64_t{SmCount()} * 16);
+          ReduceFinish<T><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(args);
+          Check(cudaGetLastError(), "reduce finish launch");
+          g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+        }
+      }
+    });
+  });
+}
+
+void LaunchAxpby(int32_t dtype, int64_t n, double ar, double ai, const void* x, double br, double bi,
+                 const void* y, void* out, cudaStream_t stream) {
+  if (n == 0) return;
+  const int64_t grid = std::min<int64_t>((n + kThreads - 1) / kThreads, int64_t{SmCount()} * 8);
+  switch (dtype) {
+    case 11:
+      AxpbyKernel<float, float><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+          n, static_cast<float>(ar), static_cast<const float*>(x), static_cast<float>(br),
+          static_cast<const float*>(y), static_cast<float*>(out));
+      break;
+    case 12:
+      AxpbyKernel<double, double><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+          n, ar, static_cast<const double*>(x), br, static_cast<const double*>(y), static_cast<double*>(out));
+      break;
+    case 15:
+      AxpbyKernel<float2, float2><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+          n, float2{static_cast<float>(ar), static_cast<float>(ai)}, static_cast<const float2*>(x),
+          float2{static_cast<float>(br), static_cast<float>(bi)}, static_cast<const float2*>(y),
+          static_cast<float2*>(out));
+      break;
+    case 18:
+      AxpbyKernel<double2, double2><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
+          n, double2{ar, ai}, static_cast<const double2*>(x), double2{br, bi},
+          static_cast<const double2*>(y), static_cast<double2*>(out));
+      break;
+    default:
+      throw InvalidArgumentError("axpby supports only F32/F64/C64/C128");
+  }
+  Check(cudaGetLastError(), "axpby launch");
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+}  // namespace t0b

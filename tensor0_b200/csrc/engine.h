@@ -1,0 +1,65 @@
+// Kernel launch interface of the map and reduce engines.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "layout.h"
+#include "plan.h"
+
+namespace t0b {
+
+using InvalidArgumentError = InvalidArgument;
+
+enum MapOp : int { kOpCopy = 0, kOpUpdate = 1, kOpAccumulation = 3 };
+
+struct MapArgs {
+  const MapRecord* recs;
+  int64_t nrec;
+  int64_t tiles_per_batch;
+  int64_t batches;
+  const void* src;
+  const void* base;
+  void* out;
+  int64_t src_size;
+  int64_t out_size;
+  const void* ca;      // accumulation: coefficient rows; update: alpha
+  int64_t ca_count;
+  const void* cb;      // update: beta
+  int64_t cb_count;
+};
+
+struct ReduceArgs {
+  const ReduceGroup* groups;
+  const ReduceRecord* records;
+  int64_t group_begin, group_end;   // wave
+  int64_t task_begin, task_end;
+  int64_t owner_begin, owner_end;
+  int64_t batches;
+  const void* src;
+  void* out;
+  void* scratch;
+  int64_t scratch_stride;           // scratch elements per batch
+  int64_t src_size;
+  int64_t out_size;
+  const void* ca;
+  int64_t ca_count;
+};
+
+extern std::atomic<uint64_t> g_kernel_launches;
+
+// Throw std::runtime_error for a failed CUDA runtime call.
+void Check(cudaError_t status, const char* what);
+
+int MapSharedBytes(const MapRecord* recs, int64_t count, int element_bytes);
+void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
+               int smem, cudaStream_t stream);
+void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream);
+void LaunchAxpby(int32_t dtype, int64_t n, double ar, double ai, const void* x, double br, double bi,
+                 const void* y, void* out, cudaStream_t stream);
+
+}  // namespace t0b

@@ -1,0 +1,340 @@
+// Grouped per-sector GEMM behind block-sparse contraction: for every coupled
+// sector g, C_g = A_g @ B_g over row-major blocks sliced from flat storage
+// (the reference loops over sectors with one XLA dot each,
+// src/tensor0/tensor/linalg.py:533-566, then concatenates, _blocks.py:83-131).
+// Here every 64x64 output tile of every sector is one task of a single
+// persistent grid.
+//
+// F64 and C128 use the FP64 tensor-core MMA (mma.sync m8n8k4 f64, "DMMA");
+// C128 uses four real products per complex product.  F32 / C64 use FP32 FMA.
+// Operands are staged with cp.async (zero-filled at edges) in two stages.
+#include "gemm.h"
+
+#include "engine.h"
+
+#include <algorithm>
+#include <vector>
+
+namespace t0b {
+namespace {
+
+constexpr int kGemmThreads = 256;
+constexpr int kTile = 64;
+
+__device__ __forceinline__ int64_t FindSector(const int64_t* table, int64_t sectors, int64_t tile) {
+  int64_t lo = 0, hi = sectors - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (table[mid * kGemmRow + 6] <= tile) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void CpAsync8(void* smem, const void* gmem, bool valid) {
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  const int bytes = valid ? 8 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(gmem), "r"(bytes));
+}
+__device__ __forceinline__ void CpAsync16(void* smem, const void* gmem, bool valid) {
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  const int bytes = valid ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem), "r"(bytes));
+}
+__device__ __forceinline__ void CpAsync4(void* smem, const void* gmem, bool valid) {
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  const int bytes = valid ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(gmem), "r"(bytes));
+}
+__device__ __forceinline__ void CpCommit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void CpWait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// D = A(8x4, row) * B(4x8, col) + D on the FP64 tensor cores.
+__device__ __forceinline__ void Dmma(double (&d)[2], double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};\n"
+               : "+d"(d[0]), "+d"(d[1])
+               : "d"(a), "d"(b));
+}
+
+struct Task {
+  int64_t m, n, k, a, b, c;
+  int64_t m0, n0;
+};
+
+__device__ __forceinline__ Task DecodeTask(const int64_t* table, int64_t sectors, int64_t tile) {
+  const int64_t s = FindSector(table, sectors, tile);
+  const int64_t* row = table + s * kGemmRow;
+  Task t;
+  t.m = row[0]; t.n = row[1]; t.k = row[2];
+  t.a = row[3]; t.b = row[4]; t.c = row[5];
+  const int64_t local = tile - row[6];
+  const int64_t tiles_n = (t.n + kTile - 1) / kTile;
+  t.m0 = (local / tiles_n) * kTile;
+  t.n0 = (local % tiles_n) * kTile;
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// FP64 / complex128 on DMMA.  8 warps as 2 (M) x 4 (N); a warp owns 32x16 of
+// the 64x64 tile = 4 x 2 fragments of 8x8.
+template <bool kComplex>
+__global__ void __launch_bounds__(kGemmThreads) DmmaGemm(const int64_t* __restrict__ table, int64_t sectors,
+                                                         int64_t tiles, const double* __restrict__ left,
+                                                         const double* __restrict__ right, double* out) {
+  // Real: K tile 16, pads keep fragment loads conflict-free.  Complex: K tile
+  // 8 complex values, stored interleaved.
+  constexpr int BK = kComplex ? 8 : 16;
+  constexpr int W = kComplex ? 2 : 1;              // doubles per element
+  constexpr int APITCH = kComplex ? (BK + 4) : (BK + 4);
+  constexpr int BPITCH = kComplex ? (kTile + 2) : (kTile + 4);
+  __shared__ __align__(16) double As[2][kTile * APITCH * W];
+  __shared__ __align__(16) double Bs[2][BK * BPITCH * W];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int wm = warp & 1, wn = warp >> 1;
+  const int fr = lane >> 2, fc = lane & 3;
+
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const Task t = DecodeTask(table, sectors, tile);
+    double acc[4][2][2] = {};
+    double acci[4][2][2] = {};
+    const int64_t ktiles = (t.k + BK - 1) / BK;
+
+    auto stage = [&](int buf, int64_t k0) {
+      if constexpr (!kComplex) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {            // A: 64 x 16 doubles
+          const int e = tid + i * kGemmThreads;
+          const int r = e >> 4, c = e & 15;
+          const bool ok = t.m0 + r < t.m && k0 + c < t.k;
+          const double* g = ok ? left + t.a + (t.m0 + r) * t.k + k0 + c : left;
+          CpAsync8(&As[buf][r * APITCH + c], g, ok);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {            // B: 16 x 64 doubles
+          const int e = tid + i * kGemmThreads;
+          const int r = e >> 6, c = e & 63;
+          const bool ok = k0 + r < t.k && t.n0 + c < t.n;
+          const double* g = ok ? right + t.b + (k0 + r) * t.n + t.n0 + c : right;
+          CpAsync8(&Bs[buf][r * BPITCH + c], g, ok);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {            // A: 64 x 8 complex
+          const int e = tid + i * kGemmThreads;
+          const int r = e >> 3, c = e & 7;
+          const bool ok = t.m0 + r < t.m && k0 + c < t.k;
+          const double* g = ok ? left + 2 * (t.a + (t.m0 + r) * t.k + k0 + c) : left;
+          CpAsync16(&As[buf][2 * (r * APITCH + c)], g, ok);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {            // B: 8 x 64 complex
+          const int e = tid + i * kGemmThreads;
+          const int r = e >> 6, c = e & 63;
+          const bool ok = k0 + r < t.k && t.n0 + c < t.n;
+          const double* g = ok ? right + 2 * (t.b + (k0 + r) * t.n + t.n0 + c) : right;
+          CpAsync16(&Bs[buf][2 * (r * BPITCH + c)], g, ok);
+        }
+      }
+      CpCommit();
+    };
+
+    if (ktiles > 0) stage(0, 0);
+    for (int64_t kt = 0; kt < ktiles; ++kt) {
+      const int buf = static_cast<int>(kt & 1);
+      if (kt + 1 < ktiles) { stage(buf ^ 1, (kt + 1) * BK); CpWait<1>(); } else { CpWait<0>(); }
+      __syncthreads();
+#pragma unroll
+      for (int kk = 0; kk < BK; kk += 4) {
+        if constexpr (!kComplex) {
+          double a[4], b[2];
+#pragma unroll
+          for (int f = 0; f < 4; ++f) a[f] = As[buf][(wm * 32 + f * 8 + fr) * APITCH + kk + fc];
+#pragma unroll
+          for (int g = 0; g < 2; ++g) b[g] = Bs[buf][(kk + fc) * BPITCH + wn * 16 + g * 8 + fr];
+#pragma unroll
+          for (int f = 0; f < 4; ++f)
+#pragma unroll
+            for (int g = 0; g < 2; ++g) Dmma(acc[f][g], a[f], b[g]);
+        } else {
+          double ar[4], ai[4], br[2], bi[2];
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            const double2 v = *reinterpret_cast<const double2*>(&As[buf][2 * ((wm * 32 + f * 8 + fr) * APITCH + kk + fc)]);
+            ar[f] = v.x; ai[f] = v.y;
+          }
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const double2 v = *reinterpret_cast<const double2*>(&Bs[buf][2 * ((kk + fc) * BPITCH + wn * 16 + g * 8 + fr)]);
+            br[g] = v.x; bi[g] = v.y;
+          }
+#pragma unroll
+          for (int f = 0; f < 4; ++f)
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+              Dmma(acc[f][g], ar[f], br[g]);
+              Dmma(acc[f][g], -ai[f], bi[g]);
+              Dmma(acci[f][g], ar[f], bi[g]);
+              Dmma(acci[f][g], ai[f], br[g]);
+            }
+        }
+      }
+      __syncthreads();
+    }
+    // Epilogue: fragment (f, g) holds rows fr, columns 2*fc + {0, 1}.
+#pragma unroll
+    for (int f = 0; f < 4; ++f) {
+      const int64_t row = t.m0 + wm * 32 + f * 8 + fr;
+      if (row >= t.m) continue;
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int64_t col = t.n0 + wn * 16 + g * 8 + 2 * fc + j;
+          if (col >= t.n) continue;
+          const int64_t at = t.c + row * t.n + col;
+          if constexpr (kComplex) {
+            reinterpret_cast<double2*>(out)[at] = double2{acc[f][g][j], acci[f][g][j]};
+          } else {
+            out[at] = acc[f][g][j];
+          }
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// FP32 / complex64: each thread owns a 4x4 block of the 64x64 tile.
+template <bool kComplex>
+__global__ void __launch_bounds__(kGemmThreads) FmaGemm(const int64_t* __restrict__ table, int64_t sectors,
+                                                        int64_t tiles, const float* __restrict__ left,
+                                                        const float* __restrict__ right, float* out) {
+  constexpr int BK = 16;
+  constexpr int W = kComplex ? 2 : 1;
+  __shared__ __align__(16) float As[BK][kTile * W + 4];
+  __shared__ __align__(16) float Bs[BK][kTile * W + 4];
+  const int tid = threadIdx.x;
+  const int tr = tid >> 4, tc = tid & 15;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const Task t = DecodeTask(table, sectors, tile);
+    float acc[4][4][W] = {};
+    for (int64_t k0 = 0; k0 < t.k; k0 += BK) {
+      for (int e = tid; e < kTile * BK; e += kGemmThreads) {    // A transposed into As[k][m]
+        const int r = e / BK, c = e % BK;
+        const bool ok = t.m0 + r < t.m && k0 + c < t.k;
+        for (int w = 0; w < W; ++w)
+          As[c][r * W + w] = ok ? left[W * (t.a + (t.m0 + r) * t.k + k0 + c) + w] : 0.0f;
+      }
+      for (int e = tid; e < kTile * BK; e += kGemmThreads) {
+        const int r = e / kTile, c = e % kTile;
+        const bool ok = k0 + r < t.k && t.n0 + c < t.n;
+        for (int w = 0; w < W; ++w)
+          Bs[r][c * W + w] = ok ? right[W * (t.b + (k0 + r) * t.n + t.n0 + c) + w] : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll 4
+      for (int kk = 0; kk < BK; ++kk) {
+        float a[4][W], b[4][W];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int w = 0; w < W; ++w) { a[i][w] = As[kk][(tr * 4 + i) * W + w]; b[i][w] = Bs[kk][(tc * 4 + i) * W + w]; }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (kComplex) {
+              acc[i][j][0] = __fmaf_rn(a[i][0], b[j][0], acc[i][j][0]);
+              acc[i][j][0] = __fmaf_rn(-a[i][1], b[j][1], acc[i][j][0]);
+              acc[i][j][1] = __fmaf_rn(a[i][0], b[j][1], acc[i][j][1]);
+              acc[i][j][1] = __fmaf_rn(a[i][1], b[j][0], acc[i][j][1]);
+            } else {
+              acc[i][j][0] = __fmaf_rn(a[i][0], b[j][0], acc[i][j][0]);
+            }
+          }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = t.m0 + tr * 4 + i;
+      if (row >= t.m) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t col = t.n0 + tc * 4 + j;
+        if (col >= t.n) continue;
+        for (int w = 0; w < W; ++w) out[W * (t.c + row * t.n + col) + w] = acc[i][j][w];
+      }
+    }
+  }
+}
+
+int SmCountGemm() {
+  static int count = [] {
+    int device = 0, sms = 148;
+    if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms;
+  }();
+  return count;
+}
+
+}  // namespace
+
+void BuildGemmTable(int64_t sectors, const int64_t* spec, int64_t* table) {
+  int64_t tiles = 0;
+  for (int64_t s = 0; s < sectors; ++s) {
+    const int64_t* in = spec + s * 6;
+    int64_t* row = table + s * kGemmRow;
+    for (int i = 0; i < 6; ++i) row[i] = in[i];
+    row[6] = tiles;
+    row[7] = 0;
+    tiles += ((in[0] + kTile - 1) / kTile) * ((in[1] + kTile - 1) / kTile);
+  }
+}
+
+void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const int64_t* device_table,
+                const void* left, const void* right, void* output, cudaStream_t stream) {
+  if (sectors < 0) throw InvalidArgument("sector count must be nonnegative");
+  if (sectors == 0) return;
+  if (host_table == nullptr || device_table == nullptr) throw InvalidArgument("GEMM table is null");
+  int64_t tiles = 0;
+  for (int64_t s = 0; s < sectors; ++s) {
+    const int64_t* row = host_table + s * kGemmRow;
+    for (int i = 0; i < 6; ++i) {
+      if (row[i] < 0) throw InvalidArgument("GEMM sizes and offsets must be nonnegative");
+    }
+    if (row[6] != tiles) throw InvalidArgument("GEMM table tile prefix is inconsistent; build it with t0b_gemm_table_build");
+    tiles += ((row[0] + kTile - 1) / kTile) * ((row[1] + kTile - 1) / kTile);
+  }
+  if (tiles == 0) return;
+  if (left == nullptr || right == nullptr || output == nullptr) throw InvalidArgument("GEMM operand is null");
+  const int64_t grid = std::min<int64_t>(tiles, int64_t{SmCountGemm()} * 4);
+  switch (dtype) {
+    case 12:
+      DmmaGemm<false><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
+          device_table, sectors, tiles, static_cast<const double*>(left), static_cast<const double*>(right),
+          static_cast<double*>(output));
+      break;
+    case 18:
+      DmmaGemm<true><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
+          device_table, sectors, tiles, static_cast<const double*>(left), static_cast<const double*>(right),
+          static_cast<double*>(output));
+      break;
+    case 11:
+      FmaGemm<false><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
+          device_table, sectors, tiles, static_cast<const float*>(left), static_cast<const float*>(right),
+          static_cast<float*>(output));
+      break;
+    case 15:
+      FmaGemm<true><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
+          device_table, sectors, tiles, static_cast<const float*>(left), static_cast<const float*>(right),
+          static_cast<float*>(output));
+      break;
+    default:
+      throw InvalidArgument("sector GEMM supports only F32/F64/C64/C128");
+  }
+  Check(cudaGetLastError(), "sector gemm launch");
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+}  // namespace t0b

@@ -1,0 +1,17 @@
+// Grouped per-sector GEMM launch interface.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace t0b {
+
+// Device table row: {m, n, k, a_off, b_off, c_off, tile_begin, 0}.
+constexpr int kGemmRow = 8;
+
+void BuildGemmTable(int64_t sectors, const int64_t* spec, int64_t* table);
+void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const int64_t* device_table,
+                const void* left, const void* right, void* output, cudaStream_t stream);
+
+}  // namespace t0b

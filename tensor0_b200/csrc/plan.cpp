@@ -1,0 +1,430 @@
+// Plan construction: validation, canonicalisation, engine selection, tiling
+// and the packed device table.
+#include "plan.h"
+
+#include "layout.h"
+
+#include <algorithm>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <numeric>
+#include <stdexcept>
+
+namespace t0b {
+namespace {
+
+constexpr uint64_t kExtentLimit = uint64_t{1} << 30;   // per-axis extent kept in int32
+constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap check
+
+// Bytes of shared memory one map tile may stage (before row padding).
+constexpr int64_t kTileBytes = 16384;
+
+// Split records so every axis extent fits in int32 and at most kMaxRank axes remain.
+std::vector<Record> SplitForDevice(const Record& record) {
+  std::vector<Record> pending{record}, done;
+  while (!pending.empty()) {
+    Record current = std::move(pending.back());
+    pending.pop_back();
+    std::size_t axis = current.shape.size();
+    for (std::size_t a = 0; a < current.shape.size(); ++a) {
+      if (current.shape[a] > kExtentLimit) { axis = a; break; }
+    }
+    if (axis != current.shape.size()) {
+      for (uint64_t start = 0; start < current.shape[axis]; start += kExtentLimit) {
+        Record piece = current;
+        piece.shape[axis] = std::min(kExtentLimit, current.shape[axis] - start);
+        piece.src_off += static_cast<int64_t>(start) * current.sstr[axis];
+        piece.dst_off += static_cast<int64_t>(start) * current.dstr[axis];
+        pending.push_back(std::move(piece));
+      }
+      continue;
+    }
+    if (current.shape.size() > static_cast<std::size_t>(kMaxRank)) {
+      // Peel the outermost map axis (or the last fiber axis if only fibers remain).
+      std::size_t peel = current.shape.size() - 1;
+      for (std::size_t a = current.shape.size(); a-- > 0;) {
+        if (!current.fiber[a]) { peel = a; break; }
+      }
+      if (current.fiber[peel]) {
+        throw std::runtime_error("reduction records with more than eight fused summed axes are unsupported");
+      }
+      for (uint64_t i = 0; i < current.shape[peel]; ++i) {
+        Record piece = current;
+        piece.src_off += static_cast<int64_t>(i) * current.sstr[peel];
+        piece.dst_off += static_cast<int64_t>(i) * current.dstr[peel];
+        piece.shape.erase(piece.shape.begin() + peel);
+        piece.sstr.erase(piece.sstr.begin() + peel);
+        piece.dstr.erase(piece.dstr.begin() + peel);
+        piece.fiber.erase(piece.fiber.begin() + peel);
+        pending.push_back(std::move(piece));
+      }
+      continue;
+    }
+    done.push_back(std::move(current));
+  }
+  std::reverse(done.begin(), done.end());
+  return done;
+}
+
+uint64_t OwnerCount(const Record& record) {
+  uint64_t owners = 1;
+  for (std::size_t a = 0; a < record.shape.size(); ++a) {
+    if (!record.fiber[a]) owners *= record.shape[a];
+  }
+  return owners;
+}
+
+// Visit every destination address of a record's map (owner) axes.
+template <typename Visit>
+void ForEachOwnerAddress(const Record& record, Visit visit) {
+  std::vector<std::size_t> axes;
+  for (std::size_t a = 0; a < record.shape.size(); ++a) {
+    if (!record.fiber[a] && record.shape[a] > 1) axes.push_back(a);
+  }
+  std::vector<uint64_t> index(axes.size(), 0);
+  int64_t address = record.dst_off;
+  for (;;) {
+    if (!visit(address)) return;
+    std::size_t k = 0;
+    for (; k < axes.size(); ++k) {
+      const std::size_t a = axes[k];
+      if (++index[k] < record.shape[a]) { address += record.dstr[a]; break; }
+      address -= static_cast<int64_t>(record.shape[a] - 1) * record.dstr[a];
+      index[k] = 0;
+    }
+    if (k == axes.size()) return;
+  }
+}
+
+// Exact pairwise-disjointness proof over the owner addresses, for sizes where
+// a bit per output element is affordable.
+bool ProveDisjoint(const std::vector<const Record*>& records, uint64_t output_size) {
+  uint64_t total = 0;
+  for (const Record* record : records) total += OwnerCount(*record);
+  if (total > output_size) return false;
+  if (output_size > kProofLimit || total > kProofLimit) return false;
+  std::vector<uint64_t> bits((output_size + 63) / 64, 0);
+  bool disjoint = true;
+  for (const Record* record : records) {
+    ForEachOwnerAddress(*record, [&](int64_t address) {
+      uint64_t& word = bits[static_cast<uint64_t>(address) >> 6];
+      const uint64_t mask = uint64_t{1} << (address & 63);
+      if (word & mask) { disjoint = false; return false; }
+      word |= mask;
+      return true;
+    });
+    if (!disjoint) return false;
+  }
+  return true;
+}
+
+int64_t CeilDiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_bytes, int64_t tile_begin) {
+  MapRecord out{};
+  out.src_off = record.src_off;
+  out.dst_off = record.dst_off;
+  out.tile_begin = tile_begin;
+  out.coef_slot = static_cast<int32_t>(slot);
+  const std::size_t rank = record.shape.size();
+  // Canonical order: axes by |destination stride|, innermost first.
+  std::size_t x = 0;
+  std::size_t y = 0;
+  for (std::size_t a = 1; a < rank; ++a) {
+    if (AbsStride(record.sstr[a]) < AbsStride(record.sstr[y])) y = a;
+  }
+  const int64_t budget = kTileBytes / element_bytes;
+  std::vector<std::size_t> rest;
+  for (std::size_t a = 0; a < rank; ++a) {
+    if (a != x && a != y) rest.push_back(a);
+  }
+  auto put = [&](int slot_index, std::size_t axis) {
+    out.n[slot_index] = static_cast<int32_t>(record.shape[axis]);
+    out.s[slot_index] = record.sstr[axis];
+    out.d[slot_index] = record.dstr[axis];
+  };
+  for (int i = 0; i < kMaxRank; ++i) { out.n[i] = 1; out.s[i] = 0; out.d[i] = 0; }
+  if (rank == 0) {
+    out.mode = kDirect;
+    out.t[0] = out.t[1] = out.t[2] = 1;
+    out.c[0] = out.c[1] = out.c[2] = 1;
+    out.nouter = 0;
+    return out;
+  }
+  put(0, x);
+  std::size_t z_axis = rank;
+  if (!rest.empty()) { z_axis = rest.front(); rest.erase(rest.begin()); }
+  if (x == y) {
+    out.mode = kDirect;
+    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], budget));
+    out.t[1] = 1;
+  } else {
+    out.mode = kTranspose;
+    put(1, y);
+    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], 64));
+    out.t[1] = static_cast<int32_t>(std::min<int64_t>(out.n[1], std::max<int64_t>(1, std::min<int64_t>(64, budget / out.t[0]))));
+  }
+  if (z_axis != rank) put(2, z_axis);
+  out.t[2] = static_cast<int32_t>(std::min<int64_t>(out.n[2], std::max<int64_t>(1, budget / (int64_t{out.t[0]} * out.t[1]))));
+  for (int i = 0; i < 3; ++i) out.c[i] = static_cast<int32_t>(CeilDiv(out.n[i], out.t[i]));
+  out.nouter = static_cast<int32_t>(rest.size());
+  for (std::size_t i = 0; i < rest.size(); ++i) put(3 + static_cast<int>(i), rest[i]);
+  return out;
+}
+
+int64_t MapTiles(const MapRecord& record) {
+  int64_t tiles = int64_t{record.c[0]} * record.c[1] * record.c[2];
+  for (int i = 0; i < record.nouter; ++i) tiles *= record.n[3 + i];
+  return tiles;
+}
+
+template <typename T>
+void Append(std::vector<int64_t>& table, const std::vector<T>& items) {
+  static_assert(sizeof(T) % 16 == 0, "device records are 16-byte multiples");
+  const std::size_t words = items.size() * sizeof(T) / sizeof(int64_t);
+  const std::size_t at = table.size();
+  table.resize(at + words);
+  if (words) std::memcpy(table.data() + at, items.data(), words * sizeof(int64_t));
+}
+
+}  // namespace
+
+Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
+               const int64_t* coefficient_records, std::size_t coefficient_count,
+               int32_t element_bytes, uint32_t flags) {
+  if (element_bytes != 4 && element_bytes != 8 && element_bytes != 16) {
+    throw InvalidArgument("element size must be 4, 8 or 16 bytes");
+  }
+  Layout layout;
+  switch (operation) {
+    case 0: case 1: layout = DecodeLayout(words, word_count, Validation::kMap); break;
+    case 3: layout = DecodeLayout(words, word_count, Validation::kAccumulation); break;
+    case 4: layout = DecodeReductionLayout(words, word_count); break;
+    default: throw InvalidArgument("unsupported stride layout operation");
+  }
+  const bool summing = operation == 3 || operation == 4;
+  if (!summing && coefficient_count != 0) {
+    throw InvalidArgument("copy and update plans take no coefficient records");
+  }
+  std::vector<int64_t> slot(layout.records.size(), -1);
+  int64_t previous = -1;
+  for (std::size_t i = 0; i < coefficient_count; ++i) {
+    const int64_t record = coefficient_records[i];
+    if (record <= previous || record < 0 || static_cast<uint64_t>(record) >= layout.records.size()) {
+      throw InvalidArgument("coefficient record indices must be increasing and in range");
+    }
+    previous = record;
+    slot[record] = static_cast<int64_t>(i);
+  }
+
+  Plan plan;
+  plan.operation = operation;
+  plan.element_bytes = element_bytes;
+  plan.flags = flags;
+  plan.source_size = layout.source_size;
+  plan.output_size = layout.output_size;
+  plan.records = layout.records.size();
+  plan.coefficient_rows = coefficient_count;
+
+  // Nonempty records in the reduce engine's canonical form (map axes ordered,
+  // not fused), split to the device limits.  Records with the same owner map
+  // share a key.
+  struct Key {
+    int64_t dst_off;
+    std::vector<std::pair<uint64_t, int64_t>> axes;
+    bool operator<(const Key& other) const {
+      return std::tie(dst_off, axes) < std::tie(other.dst_off, other.axes);
+    }
+  };
+  std::vector<Record> records;
+  std::vector<int64_t> record_slot;
+  for (const Record& original : layout.records) {
+    if (ElementCount(original) == 0) continue;
+    Record record = original;
+    Canonicalize(record, false);
+    for (Record& piece : SplitForDevice(record)) {
+      records.push_back(std::move(piece));
+      record_slot.push_back(slot[original.index]);
+    }
+  }
+  std::map<Key, std::size_t> group_of;
+  std::vector<std::vector<std::size_t>> group_members;
+  std::vector<Key> group_keys;
+  for (std::size_t i = 0; i < records.size(); ++i) {
+    const Record& record = records[i];
+    Key key{record.dst_off, {}};
+    for (std::size_t a = 0; a < record.shape.size(); ++a) {
+      if (!record.fiber[a]) key.axes.emplace_back(record.shape[a], record.dstr[a]);
+    }
+    auto found = group_of.find(key);
+    if (found == group_of.end()) {
+      found = group_of.emplace(key, group_members.size()).first;
+      group_members.emplace_back();
+      group_keys.push_back(key);
+    }
+    group_members[found->second].push_back(i);
+  }
+
+  // Distinct owner maps must be disjoint for concurrent execution: asserted
+  // by the producer, or proven here.  Copy and update rely on the reference's
+  // producer precondition of disjoint records.
+  const bool asserted = (flags & 1u) != 0;
+  bool disjoint = !summing || asserted;
+  if (!disjoint) {
+    std::vector<const Record*> maps;
+    for (const auto& members : group_members) maps.push_back(&records[members.front()]);
+    disjoint = ProveDisjoint(maps, plan.output_size);
+  }
+
+  // Engine selection: a record runs in the map engine when it has no summed
+  // axes, is the only record of its owner map, and maps are disjoint.
+  std::vector<std::size_t> map_ids;
+  std::vector<std::size_t> reduce_groups;
+  for (std::size_t g = 0; g < group_members.size(); ++g) {
+    const auto& members = group_members[g];
+    bool has_fiber = false;
+    for (std::size_t i : members) {
+      for (uint8_t f : records[i].fiber) has_fiber |= f != 0;
+    }
+    if (operation != 4 && disjoint && (!summing || (members.size() == 1 && !has_fiber))) {
+      map_ids.insert(map_ids.end(), members.begin(), members.end());
+    } else {
+      reduce_groups.push_back(g);
+    }
+  }
+  std::sort(map_ids.begin(), map_ids.end());
+
+  // Map engine.
+  std::vector<MapRecord> map_records;
+  int64_t tiles = 0;
+  uint64_t covered = 0;
+  uint64_t read_elements = 0;
+  for (std::size_t i : map_ids) {
+    Record fused = records[i];
+    Canonicalize(fused, true);
+    MapRecord record = MakeMapRecord(fused, record_slot[i], element_bytes, tiles);
+    tiles += MapTiles(record);
+    covered += ElementCount(records[i]);
+    read_elements += ElementCount(records[i]);
+    map_records.push_back(record);
+  }
+
+  // Reduce engine: groups in order of their first record; records keep their
+  // semantic order within a group.
+  std::vector<ReduceGroup> groups;
+  std::vector<ReduceRecord> reduce_records;
+  int64_t tasks = 0, owners = 0, scratch = 0;
+  std::vector<const Record*> group_maps;
+  for (std::size_t g : reduce_groups) {
+    const Key& key = group_keys[g];
+    ReduceGroup group{};
+    group.dst_off = key.dst_off;
+    group.rank = static_cast<int32_t>(key.axes.size());
+    int64_t group_owners = 1;
+    for (int a = 0; a < kMaxRank; ++a) { group.n[a] = 1; group.d[a] = 0; }
+    for (std::size_t a = 0; a < key.axes.size(); ++a) {
+      group.n[a] = static_cast<int32_t>(key.axes[a].first);
+      group.d[a] = key.axes[a].second;
+      group_owners *= static_cast<int64_t>(key.axes[a].first);
+    }
+    group.owners = group_owners;
+    group.rec_begin = static_cast<int64_t>(reduce_records.size());
+    uint64_t fiber_total = 0;
+    for (std::size_t i : group_members[g]) {
+      const Record& record = records[i];
+      ReduceRecord rr{};
+      rr.src_off = record.src_off;
+      rr.coef_slot = static_cast<int32_t>(record_slot[i]);
+      for (int a = 0; a < kMaxRank; ++a) { rr.n[a] = 1; rr.s[a] = 0; }
+      int k = 0;
+      uint64_t fiber_count = 1;
+      for (std::size_t a = 0; a < record.shape.size(); ++a) {
+        if (!record.fiber[a]) { rr.n[k] = static_cast<int32_t>(record.shape[a]); rr.s[k] = record.sstr[a]; ++k; }
+      }
+      rr.map_rank = k;
+      for (std::size_t a = 0; a < record.shape.size(); ++a) {
+        if (record.fiber[a]) {
+          rr.n[k] = static_cast<int32_t>(record.shape[a]);
+          rr.s[k] = record.sstr[a];
+          fiber_count *= record.shape[a];
+          ++k;
+        }
+      }
+      if (fiber_count > static_cast<uint64_t>(std::numeric_limits<int32_t>::max())) {
+        throw std::runtime_error("summed fibers longer than 2^31 elements are unsupported");
+      }
+      rr.fiber_rank = k - rr.map_rank;
+      rr.fiber_count = static_cast<int32_t>(fiber_count);
+      fiber_total += fiber_count;
+      read_elements += fiber_count * static_cast<uint64_t>(group_owners);
+      reduce_records.push_back(rr);
+    }
+    group.rec_end = static_cast<int64_t>(reduce_records.size());
+    const int64_t members = group.rec_end - group.rec_begin;
+    const int64_t average = std::max<int64_t>(1, static_cast<int64_t>(fiber_total) / std::max<int64_t>(1, members));
+    // Chunks of records sized for about 512 summed elements per warp task.
+    group.chunk_records = static_cast<int32_t>(std::clamp<int64_t>(CeilDiv(512, average), 1, members));
+    group.chunks = static_cast<int32_t>(CeilDiv(members, group.chunk_records));
+    group.task_begin = tasks;
+    group.owner_begin = owners;
+    group.scratch_off = scratch;
+    tasks += group.owners * group.chunks;
+    owners += group.owners;
+    scratch += group.owners * group.chunks;
+    covered += static_cast<uint64_t>(group.owners);
+    groups.push_back(group);
+    group_maps.push_back(&records[group_members[g].front()]);
+  }
+
+  // Waves of groups whose outputs are pairwise disjoint.
+  if (!groups.empty()) {
+    auto wave_for = [&](std::size_t begin, std::size_t end) {
+      Wave wave{};
+      wave.group_begin = static_cast<int64_t>(begin);
+      wave.group_end = static_cast<int64_t>(end);
+      wave.task_begin = groups[begin].task_begin;
+      wave.owner_begin = groups[begin].owner_begin;
+      wave.task_end = end < groups.size() ? groups[end].task_begin : tasks;
+      wave.owner_end = end < groups.size() ? groups[end].owner_begin : owners;
+      return wave;
+    };
+    if (disjoint) {
+      plan.waves.push_back(wave_for(0, groups.size()));
+    } else {
+      for (std::size_t g = 0; g < groups.size(); ++g) plan.waves.push_back(wave_for(g, g + 1));
+    }
+  }
+
+  plan.has_map = !map_records.empty();
+  plan.has_reduce = !groups.empty();
+  plan.map_tiles = static_cast<uint64_t>(tiles);
+  plan.tasks = static_cast<uint64_t>(tasks);
+  plan.owners = static_cast<uint64_t>(owners);
+  plan.scratch = static_cast<uint64_t>(scratch);
+  // Every output element is written by the map engine exactly once.
+  plan.full_coverage = disjoint && !plan.has_reduce && covered == plan.output_size;
+  const uint64_t out_bytes = plan.output_size * element_bytes;
+  plan.bytes_moved = read_elements * element_bytes + out_bytes + (operation == 1 ? out_bytes : 0);
+
+  TableHeader header{};
+  header.version = kTableVersion;
+  header.map_records = static_cast<int64_t>(map_records.size());
+  header.map_tiles = tiles;
+  header.groups = static_cast<int64_t>(groups.size());
+  header.reduce_records = static_cast<int64_t>(reduce_records.size());
+  header.tasks = tasks;
+  header.owners = owners;
+  header.scratch = scratch;
+  plan.table.assign(sizeof(TableHeader) / sizeof(int64_t), 0);
+  header.map_offset = static_cast<int64_t>(plan.table.size());
+  Append(plan.table, map_records);
+  header.group_offset = static_cast<int64_t>(plan.table.size());
+  Append(plan.table, groups);
+  header.reduce_offset = static_cast<int64_t>(plan.table.size());
+  Append(plan.table, reduce_records);
+  std::memcpy(plan.table.data(), &header, sizeof(header));
+  return plan;
+}
+
+}  // namespace t0b

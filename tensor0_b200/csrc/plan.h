@@ -1,0 +1,122 @@
+// The packed per-call descriptor table and the plan that owns its host copy.
+//
+// One table replaces the reference's per-record owner/fiber words
+// (crates/tensor0-py/native/layout/descriptor.cc:237-290) and its one launch
+// per record (crates/tensor0-cuda12/native/cuda/execute/sum.cuh:15-57):
+//
+//   map engine    — injective, mutually disjoint records without summed axes
+//                   (copy, permute-accumulate, update).  Each record is cut
+//                   into tiles: a box over its destination-innermost axis X,
+//                   its source-innermost axis Y and one more destination axis
+//                   Z; the remaining axes are enumerated per tile.  A tile is
+//                   staged through shared memory so both the reads and the
+//                   writes are coalesced.  All tiles of all records form one
+//                   grid.
+//   reduce engine — records with summed (fiber) axes or shared outputs
+//                   (partial trace, general accumulation).  Records with the
+//                   same output map form a group; pass 1 reduces chunks of a
+//                   group's records per output owner with warp shuffles into
+//                   scratch, pass 2 combines the chunks in record order.
+#pragma once
+
+#include <cstdint>
+#include <vector>
+
+namespace t0b {
+
+constexpr int kMaxRank = 8;
+
+// Map-engine record (device layout; shared by host and device code).
+struct alignas(16) MapRecord {
+  int64_t src_off;
+  int64_t dst_off;
+  int64_t tile_begin;   // first tile of this record within one batch
+  int64_t s[kMaxRank];  // source strides:      X, Y, Z, outer...
+  int64_t d[kMaxRank];  // destination strides: X, Y, Z, outer...
+  int32_t n[kMaxRank];  // extents:             X, Y, Z, outer...
+  int32_t t[3];         // tile extents of X, Y, Z
+  int32_t c[3];         // chunks along X, Y, Z
+  int32_t nouter;       // outer axes after the three box axes
+  int32_t mode;         // kTranspose or kDirect
+  int32_t coef_slot;    // coefficient row, or -1 for factor one
+  int32_t pad_;
+};
+
+enum MapMode : int32_t { kTranspose = 0, kDirect = 1 };
+
+// Reduce-engine group of records that write the same output map.
+struct alignas(16) ReduceGroup {
+  int64_t dst_off;
+  int64_t d[kMaxRank];  // destination strides of the map (owner) axes
+  int32_t n[kMaxRank];  // extents of the map axes
+  int32_t rank;         // map axes
+  int32_t chunks;       // record chunks (pass-1 partials per owner)
+  int64_t owners;
+  int64_t rec_begin;    // [rec_begin, rec_end) in the ReduceRecord array
+  int64_t rec_end;
+  int64_t task_begin;   // first pass-1 task (one task = one owner x one chunk)
+  int64_t owner_begin;  // prefix of owners over groups (pass-2 threads)
+  int64_t scratch_off;  // partial of (chunk, owner) at scratch_off + chunk * owners + owner
+  int32_t chunk_records;
+  int32_t pad_;
+};
+
+struct alignas(16) ReduceRecord {
+  int64_t src_off;
+  int64_t s[kMaxRank];  // source strides: map axes (group order) then fiber axes
+  int32_t n[kMaxRank];  // extents: map axes then fiber axes
+  int32_t map_rank;
+  int32_t fiber_rank;
+  int32_t coef_slot;
+  int32_t fiber_count;
+};
+
+struct TableHeader {
+  int64_t version;          // kTableVersion
+  int64_t map_records;
+  int64_t map_tiles;        // tiles per batch
+  int64_t map_offset;       // word offset of the MapRecord array
+  int64_t groups;
+  int64_t group_offset;
+  int64_t reduce_records;
+  int64_t reduce_offset;
+  int64_t tasks;            // pass-1 tasks per batch
+  int64_t owners;           // pass-2 threads per batch
+  int64_t scratch;          // scratch elements per batch
+  int64_t reserved[5];
+};
+
+constexpr int64_t kTableVersion = 0x7430620001;
+
+struct Wave {               // consecutive groups that may run concurrently
+  int64_t group_begin, group_end;
+  int64_t task_begin, task_end;
+  int64_t owner_begin, owner_end;
+};
+
+struct Plan {
+  int32_t operation = 0;
+  int32_t element_bytes = 0;
+  uint32_t flags = 0;
+  uint64_t source_size = 0;
+  uint64_t output_size = 0;
+  uint64_t records = 0;
+  uint64_t coefficient_rows = 0;
+  bool full_coverage = false;    // the map engine writes every output element
+  bool has_map = false;
+  bool has_reduce = false;
+  uint64_t map_tiles = 0;
+  uint64_t tasks = 0;
+  uint64_t owners = 0;
+  uint64_t scratch = 0;
+  uint64_t bytes_moved = 0;      // algorithmic bytes of one batch
+  std::vector<Wave> waves;       // reduce-engine waves, in order
+  std::vector<int64_t> table;    // packed device table (host words)
+};
+
+// Build a plan; throws InvalidArgument / std::runtime_error.
+Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
+               const int64_t* coefficient_records, std::size_t coefficient_count,
+               int32_t element_bytes, uint32_t flags);
+
+}  // namespace t0b
