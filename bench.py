@@ -1,0 +1,365 @@
+#!/usr/bin/env python
+"""Benchmark: block-permute / accumulate HBM GB/s on B200.
+
+Workload (one step, per rank): the U(1) 4-leg TensorMap hom((v, v), (v, v)),
+each leg carrying charges -4..4 with degeneracy round(64 exp(-q^2 / 8))
+(N = 1,023,777,634 elements, 489 sub-blocks, 17 blocks), synthetic N(0, 1)
+data from a seed:
+  1. y = permute(x, ((2, 0), (3, 1)))          (alpha = 1, beta = 0)
+  2. z = 1 * permute(x, ((2, 0), (3, 1))) + 1 * z   (beta = 1 accumulate)
+Algorithmic bytes per step: 2 N s + 3 N s (s = element size).  Inputs (4 GB
+for f32) exceed the 126 MB L2, so no flush is needed between steps.
+
+Multi-GPU: one process per GPU; the storage batch axis is partitioned (rank r
+owns batch element r, the reference's own data-parallel axis), so per-GPU work
+is fixed as N grows (weak scaling) and the data path has no collective.
+
+``--impl reference`` times the reference's own CPU executors (oracle/_ref,
+compiled from the reference sources) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "block-permute/accumulate HBM GB/s"
+UNIT = "GB/s"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--dtype", choices=("f32", "c64"), default="f32")
+    p.add_argument("--e2e-steps", type=int, default=None, help="end-to-end steps (default: min(steps, 5))")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--scale", type=int, default=64,
+                   help="leg degeneracy scale (64 = the benchmark workload; smaller values for profiling)")
+    return p.parse_args()
+
+
+def workload_space(scale: int = 64):
+    from tensor0_b200.structure import U1Irrep, hom, space
+    degs = {q: int(round(scale * np.exp(-q * q / 8))) for q in range(-4, 5)}
+    v = space(U1Irrep, degs)
+    return hom((v, v), (v, v)), degs
+
+
+def workload_config(args, elements: int = 1023777634):
+    return {"workload": "u1-4leg permute((2,0),(3,1)) + beta=1 accumulate",
+            "legs": f"U1 q=-4..4, deg round({args.scale} exp(-q^2/8))", "elements": elements,
+            "sub_blocks": 489, "dtype": args.dtype, "l2": "inputs larger than the 126 MB L2, no flush",
+            "parallelism": f"dp{args.gpus} over storage batch"}
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's own executors on a bounded sample.
+
+
+SAMPLE_SCALE = 40     # degeneracies round(40 exp(-q^2/8)): same structure, ~1/6.6 of the elements
+
+
+def cpu_reference_steps(dtype_name: str, steps: int, warmup: int, threads: int):
+    """Time the compiled reference (oracle/_ref) on the sample workload; GB/s."""
+    from oracle import ref
+    from tensor0_b200.structure import degeneracy_structure
+    from tensor0_b200.tensor_map import permute_plan
+    h, degs = workload_space(SAMPLE_SCALE)
+    plan = permute_plan(h, (2, 0), (3, 1))
+    n = degeneracy_structure(h).total_dim
+    dtype = np.float32 if dtype_name == "f32" else np.complex64
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal(n).astype(np.float32)
+    if dtype == np.complex64:
+        x = (x + 1j * rng.standard_normal(n).astype(np.float32)).astype(np.complex64)
+    z = np.zeros(plan.output_size, dtype)
+    y = np.empty(plan.output_size, dtype)
+    records = np.arange(len(plan.transform.src))
+    ones = [np.float32(1.0)] * len(records)
+    ref.set_threads(threads)
+    item = np.dtype(dtype).itemsize
+    step_bytes = 5 * n * item
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        ref.accumulation(plan.words, x, plan.output_size, ones, records, outputs_disjoint=True, threads=threads,
+                         out=y)
+        ref.update(plan.words, x, z, np.float32(1.0), np.float32(1.0), threads=threads, out=z)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    seconds = sum(times)
+    sample = (f"u1-4leg deg round({SAMPLE_SCALE} exp(-q^2/8)) {dict(degs)}, N={n} ({step_bytes / 1e9:.2f} GB "
+              f"algorithmic per step), {steps} steps")
+    return step_bytes * steps / seconds / 1e9, seconds * 1e3 / steps, sample
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps = max(1, min(args.steps, 10))
+    value, ms, sample = cpu_reference_steps(args.dtype, steps, max(1, min(args.warmup, 2)), threads)
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.dtype, "data": "synthetic N(0,1), seeded",
+            "config": workload_config(args), "impl": "reference",
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU clocks during the timed region.
+
+
+class ClockSampler:
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=5)
+
+    def summary(self):
+        samples = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != 8 or not self.uuid.lower().endswith(parts[0].lower()[-12:]):
+                continue
+            try:
+                samples.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for s in samples for n, v in zip(names, s[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(s[0] for s in samples), "sm_max_mhz": max(s[1] for s in samples),
+                "power_w_max": max(s[2] for s in samples), "reasons": reasons, "samples": len(samples)}
+
+
+def device_uuid(index: int) -> str:
+    import torch
+    try:
+        return str(torch.cuda.get_device_properties(index).uuid)
+    except Exception:
+        return ""
+
+
+# ---------------------------------------------------------------------------
+# GPU arm.
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        peaks = json.loads(path.read_text())
+        return float(peaks["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "map_kernel_u1_permute_accumulate.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_update_launch_full_size:"):
+            try:
+                return float(line.split(":", 1)[1])
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from tensor0_b200 import _native, stride
+    from tensor0_b200.structure import degeneracy_structure
+    from tensor0_b200.tensor_map import TensorMap, add_transform, permute, permute_plan
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+
+    h, _ = workload_space(args.scale)
+    plan = permute_plan(h, (2, 0), (3, 1))
+    n = degeneracy_structure(h).total_dim
+    tdtype = torch.float32 if args.dtype == "f32" else torch.complex64
+    item = 4 if args.dtype == "f32" else 8
+    acc_plan = plan.engine_plan(_native.OP_ACCUMULATION, tdtype)
+    upd_plan = plan.engine_plan(_native.OP_UPDATE, tdtype)
+
+    # Synthetic N(0, 1) storage for this rank's batch element.
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    x = torch.randn(n, generator=gen, device=device, dtype=tdtype)
+    z = torch.randn(n, generator=gen, device=device, dtype=tdtype)
+    y = torch.empty_like(x)
+    ones = torch.ones(len(plan.transform.src), dtype=torch.float32, device=device)
+    alpha = torch.ones(1, dtype=torch.float32, device=device)
+    beta = torch.ones(1, dtype=torch.float32, device=device)
+
+    def step():
+        stride.execute_accumulation(x, acc_plan, ones, out=y)
+        stride.execute_update(x, z, alpha, beta, upd_plan, out=z)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    stream = torch.cuda.current_stream(device)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    launches0 = stride.kernel_launches()
+    with ClockSampler(device_uuid(local_rank)) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for k in range(args.steps):
+            marks[2 * k].record(stream)
+            stride.execute_accumulation(x, acc_plan, ones, out=y)
+            marks[2 * k + 1].record(stream)
+            stride.execute_update(x, z, alpha, beta, upd_plan, out=z)
+        marks[2 * args.steps].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    launches = stride.kernel_launches() - launches0
+    elapsed = start.elapsed_time(end)
+    permute_ms = [marks[2 * k].elapsed_time(marks[2 * k + 1]) for k in range(args.steps)]
+    update_ms = [marks[2 * k + 1].elapsed_time(marks[2 * k + 2]) for k in range(args.steps)]
+    if world > 1:
+        t = torch.tensor([elapsed], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+    step_bytes = 5 * n * item
+    value = world * step_bytes * args.steps / (elapsed / 1e3) / 1e9
+
+    peak, peak_kind = load_peaks()
+    update_bytes = 3 * n * item
+    permute_bytes = 2 * n * item
+    achieved = update_bytes / (statistics.mean(update_ms) / 1e3) / 1e9
+    permute_achieved = permute_bytes / (statistics.mean(permute_ms) / 1e3) / 1e9
+
+    # End to end through the public API with host buffers: every step copies
+    # x and z in from pinned memory and reads y and z back.
+    e2e_steps = args.e2e_steps or min(args.steps, 5)
+    x_host = x.cpu().pin_memory()
+    z_host = z.cpu().pin_memory()
+    y_back = torch.empty_like(x_host).pin_memory()
+    z_back = torch.empty_like(z_host).pin_memory()
+    xs = TensorMap(h, torch.empty_like(x))
+    zs = TensorMap(plan.dst, torch.empty_like(z))
+    permute(xs, ((2, 0), (3, 1)))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        xs.data.copy_(x_host, non_blocking=True)
+        zs.data.copy_(z_host, non_blocking=True)
+        ys = permute(xs, ((2, 0), (3, 1)))
+        zs = add_transform(zs, xs, ((2, 0), (3, 1)), 1.0, 1.0, inplace=True)
+        y_back.copy_(ys.data, non_blocking=True)
+        z_back.copy_(zs.data, non_blocking=True)
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e_elapsed = e_start.elapsed_time(e_end)
+    if world > 1:
+        t = torch.tensor([e_elapsed], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_elapsed = float(t.item())
+    e2e_value = world * step_bytes * e2e_steps / (e_elapsed / 1e3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        value_cpu, ms_cpu, sample = cpu_reference_steps(args.dtype, 3, 1, threads)
+        cpu = {"value": round(value_cpu, 3), "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
+            "data": "synthetic N(0,1) from seed (no dataset)", "config": workload_config(args, n),
+            "roofline": {"bound": "hbm", "kernel": "MapKernel<update> (beta=1 accumulate launch)",
+                         "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": load_traffic(),
+                         "algorithmic_bytes_per_launch": update_bytes,
+                         "permute_launch": {"achieved": round(permute_achieved, 2),
+                                            "frac": round(permute_achieved / peak, 4),
+                                            "algorithmic_bytes_per_launch": permute_bytes}},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "steps": e2e_steps,
+                    "h2d_bytes_per_step": 2 * n * item, "d2h_bytes_per_step": 2 * n * item},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -105,10 +105,11 @@ def copy(words, source: np.ndarray, output_size: int, threads: int = 1) -> np.nd
 
 
 def accumulation(words, source: np.ndarray, output_size: int, coefficients=(), coefficient_records=(),
-                 outputs_disjoint: bool = False, threads: int = 1) -> np.ndarray:
+                 outputs_disjoint: bool = False, threads: int = 1, out: np.ndarray | None = None) -> np.ndarray:
     source = np.ascontiguousarray(source)
     batches = int(np.prod(source.shape[:-1], dtype=np.int64))
-    out = np.full((*source.shape[:-1], output_size), 7, dtype=source.dtype)
+    if out is None:
+        out = np.full((*source.shape[:-1], output_size), 7, dtype=source.dtype)
     words = _words(words)
     records, arrays, pointers, dtypes, counts = _coefficients(list(coefficients), coefficient_records)
     _call(lib().t0ref_accumulation, ctypes.c_int(_DTYPES[source.dtype]), words.ctypes.data_as(c_i64p),

@@ -430,8 +430,8 @@ def degeneracy_structure(space: HomSpace) -> DegeneracyStructure:
         if space.numin:
             s[:, :, space.numout:] = cd[None, :, :]
             z[:, :, space.numout:] = _row_major(cd)[None, :, :]
-        sizes.append(s.reshape(-1, rank))
-        strides.append(z.reshape(-1, rank))
+        sizes.append(s.reshape(nr * nc, rank))
+        strides.append(z.reshape(nr * nc, rank))
         rows_out.append(row_dim)
         cols_out.append(col_dim)
         starts.append(start)

@@ -182,7 +182,7 @@ def permute(tensor: TensorMap, p) -> TensorMap:
     plan = permute_plan(tensor.space, p_codomain, p_domain)
     engine = plan.engine_plan(_native.OP_ACCUMULATION, tensor.data.dtype)
     real = torch.float32 if tensor.data.dtype in (torch.float32, torch.complex64) else torch.float64
-    coefficients = torch.as_tensor(plan.transform.coeff, dtype=real, device=tensor.data.device)
+    coefficients = _device_constant(plan.transform.coeff, real, tensor.data.device)
     out = stride.execute_accumulation(tensor.data.contiguous(), engine, coefficients)
     return TensorMap(plan.dst, out)
 
@@ -204,14 +204,30 @@ def add_transform(destination: TensorMap, source: TensorMap, p, alpha=1, beta=1,
     return TensorMap(destination.space, result)
 
 
+_CONSTANTS: dict = {}
+
+
+def _device_constant(values, dtype: torch.dtype, device) -> torch.Tensor:
+    """Device copy of small host constants (coefficient rows), made once per
+    value, dtype and device so that repeated calls issue no host copies."""
+    array = np.ascontiguousarray(np.asarray(values))
+    key = (array.tobytes(), array.shape, str(array.dtype), dtype, str(device))
+    tensor = _CONSTANTS.get(key)
+    if tensor is None:
+        if len(_CONSTANTS) > 4096:
+            _CONSTANTS.clear()
+        tensor = torch.as_tensor(array).to(dtype=dtype, device=device)
+        _CONSTANTS[key] = tensor
+    return tensor
+
+
 def _coefficient(value, storage: torch.Tensor) -> torch.Tensor:
     real = torch.float32 if storage.dtype in (torch.float32, torch.complex64) else torch.float64
     if isinstance(value, complex) and value.imag != 0:
         if not storage.is_complex():
             raise ValueError("complex coefficient on real storage")
-        return torch.tensor([value], dtype=storage.dtype, device=storage.device)
-    return torch.tensor([complex(value).real if isinstance(value, complex) else value], dtype=real,
-                        device=storage.device)
+        return _device_constant([value], storage.dtype, storage.device)
+    return _device_constant([complex(value).real if isinstance(value, complex) else value], real, storage.device)
 
 
 # ---------------------------------------------------------------------------
@@ -299,7 +315,7 @@ def tensortrace(tensor: TensorMap, *, axes, output) -> TensorMap:
     plan = trace_plan(tensor.space, left, right, out_codomain, out_domain)
     engine = plan.engine_plan(tensor.data.dtype)
     real = torch.float32 if tensor.data.dtype in (torch.float32, torch.complex64) else torch.float64
-    coefficients = torch.as_tensor(plan.coefficients, dtype=real, device=tensor.data.device)
+    coefficients = _device_constant(plan.coefficients, real, tensor.data.device)
     out = stride.execute_reduction(tensor.data.contiguous(), engine, coefficients)
     return TensorMap(plan.dst, out)
 

@@ -1,0 +1,139 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol the header
+declares, and its plan validation reproduces the reference's error classes and
+messages (crates/tensor0-py/native/layout/descriptor.cc:14-165; errors map to
+InvalidArgument = status 1, ffi/errors.h:12-24).  No compute call runs here."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from tensor0_b200 import _native, build, stride
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "tensor0_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _native.lib()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(t0b_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert len(names) >= 17
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_native.SIGNATURES)
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.t0b_version()
+
+
+def plan_error(operation, words, element_bytes=8, records=()):
+    with pytest.raises(ValueError) as error:
+        stride.Plan(operation, np.asarray(words, np.int64), element_bytes=element_bytes, coefficient_records=records)
+    return str(error.value)
+
+
+@pytest.mark.parametrize("words, message", [
+    ([2, 1, 1, 0], "unsupported native layout version"),
+    ([1, -1, 1, 0], "layout size or offset is negative"),
+    ([1, 4, 4, 5], "layout record count exceeds descriptor length"),
+    ([1, 4], "layout descriptor is truncated"),
+    ([1, 4, 4, 1, 1, 0, 0], "layout rank exceeds descriptor length"),
+    ([1, 4, 4, 1, 9, 0, 0, 1, 1, 1], "layout rank exceeds descriptor length"),
+    ([1, 4, 4, 1, 1, 0, 0, 4, 1, 1, 7], "layout descriptor has trailing words"),
+    ([1, 4, 4, 1, 1, 0, 0, 5, 1, 1], "source address exceeds storage"),
+    ([1, 4, 4, 1, 1, 0, 0, 2, -1, 1], "source address precedes storage"),
+    ([1, 4, 4, 1, 1, 0, 1, 4, 1, 1], "destination address exceeds storage"),
+    ([1, 4, 4, 1, 2, 0, 0, 2, 2, 1, 1, 1, 1], "destination strides do not prove an injective view"),
+])
+def test_copy_descriptor_validation(lib, words, message):
+    assert message in plan_error(_native.OP_COPY, words)
+    from oracle import ref
+    if ref.available():
+        # The compiled reference rejects the same words with the same message.
+        with pytest.raises(ref.ReferenceError) as error:
+            ref.prepare_layout(0, words)
+        assert error.value.status == 1 and message in str(error.value)
+
+
+def test_accumulation_allows_zero_stride_fibers_but_not_collisions(lib):
+    fiber = [1, 4, 2, 1, 2, 0, 0, 2, 2, 2, 1, 1, 0]
+    plan = stride.Plan(_native.OP_ACCUMULATION, np.asarray(fiber), element_bytes=8)
+    assert plan.output_size == 2
+    colliding = [1, 4, 4, 1, 2, 0, 0, 2, 2, 1, 1, 1, 1]
+    assert "accumulation cannot prove injective output owners" in plan_error(_native.OP_ACCUMULATION, colliding)
+
+
+def test_coefficient_records_must_increase(lib):
+    words = [1, 4, 4, 2, 1, 0, 0, 2, 1, 1, 1, 2, 2, 2, 1, 1]
+    assert "coefficient record indices must be increasing" in plan_error(_native.OP_ACCUMULATION, words,
+                                                                         records=[1, 0])
+    assert "coefficient record indices" in plan_error(_native.OP_ACCUMULATION, words, records=[2])
+
+
+def test_reduction_validation(lib):
+    words = stride.encode_reduction_layout(
+        [stride.AffineRecord((2, 2), (2, 1), 0, (1, 0), 0)], output_shapes=[(2, 1)],
+        reduction_axes=[(False, True)], source_size=4, output_size=2)
+    plan = stride.Plan(_native.OP_REDUCTION, words, element_bytes=8)
+    assert plan.scratch_elements > 0
+    bad = words.copy()
+    bad[-1] = 2
+    assert "reduction layout axis flag is not boolean" in plan_error(_native.OP_REDUCTION, bad)
+    wrong = stride.encode_reduction_layout(
+        [stride.AffineRecord((2, 2), (2, 1), 0, (1, 0), 0)], output_shapes=[(2, 2)],
+        reduction_axes=[(False, True)], source_size=4, output_size=2)
+    assert "reduction input/output shapes do not match axis roles" in plan_error(_native.OP_REDUCTION, wrong)
+
+
+def test_plan_lifecycle_counters(lib):
+    created = lib.t0b_plan_created_count()
+    destroyed = lib.t0b_plan_destroyed_count()
+    plan = stride.Plan(_native.OP_COPY, np.asarray([1, 4, 4, 1, 1, 0, 0, 4, 1, 1]), element_bytes=4)
+    assert plan.info["full_coverage"] == 1
+    assert lib.t0b_plan_created_count() == created + 1
+    del plan
+    assert lib.t0b_plan_destroyed_count() == destroyed + 1
+
+
+def test_unknown_dtype_is_rejected_before_any_device_work(lib):
+    plan = stride.Plan(_native.OP_COPY, np.asarray([1, 4, 4, 1, 1, 0, 0, 4, 1, 1]), element_bytes=4)
+    err = _native.error_buffer()
+    status = lib.t0b_copy(plan._handle, 9, None, None, 1, None, None, err, len(err))
+    assert status == 1 and b"F32/F64/C64/C128" in err.value
+    status = lib.t0b_copy(plan._handle, _native.F64, None, None, 1, None, None, err, len(err))
+    assert status == 1 and b"element size" in err.value
+
+
+def test_overlapping_buffers_are_rejected(lib):
+    plan = stride.Plan(_native.OP_COPY, np.asarray([1, 4, 4, 1, 1, 0, 0, 4, 1, 1]), element_bytes=4)
+    err = _native.error_buffer()
+    table = ctypes.c_void_p(0x20000)
+    status = lib.t0b_copy(plan._handle, _native.F32, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x1008), 1,
+                          table, None, err, len(err))
+    assert status == 1 and b"overlap" in err.value
+
+
+def test_map_tiling_covers_every_element(lib):
+    """The packed table's tiles account for every element of every record."""
+    from tensor0_b200.structure import U1Irrep, hom, space
+    from tensor0_b200.tensor_map import permute_plan
+    v = space(U1Irrep, {-2: 4, -1: 8, 0: 12, 1: 8, 2: 4})
+    plan = permute_plan(hom((v, v), (v, v)), (1, 0), (3, 2))
+    import torch
+    engine = plan.engine_plan(_native.OP_ACCUMULATION, torch.float64)
+    assert engine.info["full_coverage"] == 1
+    assert engine.info["kernels_per_call"] == 1
+    assert engine.info["records"] == 85
