@@ -130,56 +130,69 @@ def run_reference(args, rank: int):
 
 
 class ClockSampler:
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """SM clock, power and throttle reasons sampled every 10 ms through NVML
+    while the timed region runs (reads only; no setting is changed)."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, uuid: str):
         self.uuid = uuid
-        self.lines: list[str] = []
-        self.proc = None
+        self.samples: list[tuple[float, float, float, int]] = []
+        self.stop = threading.Event()
         self.thread = None
+        self.handle = None
+        self.nvml = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            for candidate in (self.uuid, "GPU-" + self.uuid):
+                try:
+                    self.handle = pynvml.nvmlDeviceGetHandleByUUID(candidate)
+                    break
+                except pynvml.NVMLError:
+                    continue
+            if self.handle is not None:
+                self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+                self.thread = threading.Thread(target=self._run, daemon=True)
+                self.thread.start()
+        except Exception:
+            self.handle = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nvml = self.nvml
+        reasons = getattr(nvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(self.handle, nvml.NVML_CLOCK_SM)
+                power = nvml.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                mask = reasons(self.handle)
+                util = nvml.nvmlDeviceGetUtilizationRates(self.handle).gpu
+                self.samples.append((float(sm), power, float(util), int(mask)))
+            except Exception:
+                pass
+            self.stop.wait(0.01)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread:
-                self.thread.join(timeout=5)
+        self.stop.set()
+        if self.thread:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        samples = []
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) != 8 or not self.uuid.lower().endswith(parts[0].lower()[-12:]):
-                continue
-            try:
-                samples.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
-            except ValueError:
-                continue
-        if not samples:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({n for s in samples for n, v in zip(names, s[3]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(s[0] for s in samples), "sm_max_mhz": max(s[1] for s in samples),
-                "power_w_max": max(s[2] for s in samples), "reasons": reasons, "samples": len(samples)}
+        mask = 0
+        for s in self.samples:
+            mask |= s[3]
+        reasons = sorted(name for bit, name in self.REASONS.items() if mask & bit)
+        return {"sm_mhz": statistics.median(s[0] for s in self.samples), "sm_max_mhz": float(self.max_mhz),
+                "power_w_max": round(max(s[1] for s in self.samples), 1), "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml, 10 ms"}
 
 
 def device_uuid(index: int) -> str:

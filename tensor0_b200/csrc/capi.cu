@@ -121,7 +121,7 @@ void RunMap(const t0b_plan* plan, int op, int32_t dtype, int32_t ca_dtype, int32
   args.ca_count = ca_count;
   args.cb = cb;
   args.cb_count = cb_count;
-  t0b::LaunchMap(op, dtype, ca_dtype, cb_dtype, args, plan->map_smem, stream);
+  t0b::LaunchMap(op, dtype, ca_dtype, cb_dtype, args, plan->map_smem, plan->plan.map_wide, stream);
 }
 
 void RunReduce(const t0b_plan* plan, int32_t dtype, int32_t ca_dtype, const void* src, void* out,
@@ -199,12 +199,6 @@ void Sum(const t0b_plan* plan, int32_t operation, int32_t dtype, const void* sou
 }
 
 }  // namespace
-
-namespace t0b {
-void Check(cudaError_t status, const char* what) {
-  if (status != cudaSuccess) throw std::runtime_error(std::string("CUDA ") + what + ": " + cudaGetErrorString(status));
-}
-}  // namespace t0b
 
 extern "C" {
 

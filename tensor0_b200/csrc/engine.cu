@@ -2,11 +2,15 @@
 // kernel and the two-pass segmented reduction for partial traces.
 //
 // The map kernel is one persistent grid over every tile of every record of
-// every batch.  A tile is a box over the record's destination-innermost axis
-// X, its source-innermost axis Y and one further axis Z; it is read with lanes
-// running along Y (coalesced source reads), staged in shared memory and
-// written with lanes running along X (coalesced destination writes).  When X
-// and Y coincide the tile is copied row by row without staging.
+// every batch; each CTA walks a contiguous range of tiles.  A tile is a box
+// over the record's destination-innermost axis X, its source-innermost axis Y
+// and one further axis Z.  One thread decodes the tile (record cursor, chunk
+// coordinates, outer axes) into shared memory; then the CTA reads the tile
+// with lanes running along Y (coalesced source reads), stages it in shared
+// memory and writes it with lanes running along X (coalesced destination
+// writes).  When X and Y coincide the tile is copied row by row.  Rows are
+// handled several at a time per warp so each thread keeps several loads in
+// flight before it stores.
 #include "engine.h"
 
 #include "arith.cuh"
@@ -22,106 +26,93 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 4;   // rows per warp step
 
-// Division by a runtime divisor below 2^24 for dividends below 2^24.
+// Division by a runtime divisor in [1, 2^24) for dividends below 2^24.
 struct FastDiv {
-  uint32_t d, m, l;
-  __device__ __forceinline__ explicit FastDiv(uint32_t divisor) : d(divisor) {
-    l = 32 - __clz(divisor - 1);                         // ceil(log2(d)), d >= 1
+  uint32_t m, l;
+  __device__ __forceinline__ explicit FastDiv(uint32_t divisor) {
+    l = 32 - __clz(divisor - 1);                         // ceil(log2(divisor))
     const uint64_t one = 1;
     m = static_cast<uint32_t>(((one << 32) * ((one << l) - divisor)) / divisor + 1);
   }
-  __device__ __forceinline__ uint32_t Div(uint32_t n) const {
-    return (__umulhi(n, m) + n) >> l;
-  }
+  __device__ __forceinline__ uint32_t Div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
 };
 
-// Load one MapRecord field set into registers.
-struct TileView {
-  int64_t so, dof;           // source / destination element offsets of the tile origin
-  int64_t sx, sy, sz, dx, dy, dz;
-  int ex, ey, ez;            // actual tile extents
-  int px, ty;                // shared-memory pitch along X and tile extent along Y
-  int mode;
-  int slot;
+// A decoded tile, shared by the CTA.  In-tile offsets use Off (int32 unless
+// the plan marked a record wide).
+template <typename Off>
+struct TileState {
+  int64_t so, dof;        // element offsets of the tile origin, batch included
+  Off sx, sy, sz, dx, dy, dz;
+  int ex, ey, ez;         // tile extents (edge tiles are smaller)
+  int px, pz;             // shared-memory pitches: along Y (odd, >= ex) and along Z
+  int mode, slot;
+  int64_t batch;
 };
 
-__device__ __forceinline__ int64_t FindRecord(const MapRecord* recs, int64_t count, int64_t local) {
-  int64_t lo = 0, hi = count - 1;
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if (recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
+// Thread 0 only: advance the record cursor to the tile and decode it.
+template <typename Off>
+__device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64_t& cursor, TileState<Off>& s) {
+  const int64_t batch = tile / a.tiles_per_batch;
+  const int64_t local = tile - batch * a.tiles_per_batch;
+  if (cursor < 0 || a.recs[cursor].tile_begin > local) {
+    int64_t lo = 0, hi = a.nrec - 1;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (a.recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
+    }
+    cursor = lo;
   }
-  return lo;
-}
-
-__device__ __forceinline__ TileView DecodeTile(const MapRecord& r, int64_t local, int64_t batch,
-                                               int64_t src_size, int64_t out_size) {
-  TileView v;
-  int64_t q = local - r.tile_begin;
-  const int c0 = r.c[0], c1 = r.c[1], c2 = r.c[2];
-  const int cx = static_cast<int>(q % c0); q /= c0;
-  const int cy = static_cast<int>(q % c1); q /= c1;
-  const int cz = static_cast<int>(q % c2); q /= c2;
-  v.so = r.src_off + batch * src_size;
-  v.dof = r.dst_off + batch * out_size;
+  while (cursor + 1 < a.nrec && a.recs[cursor + 1].tile_begin <= local) ++cursor;
+  const MapRecord& r = a.recs[cursor];
+  uint32_t q = static_cast<uint32_t>(local - r.tile_begin);
+  const uint32_t c0 = r.c[0], c1 = r.c[1], c2 = r.c[2];
+  const uint32_t cx = q % c0; q /= c0;
+  const uint32_t cy = q % c1; q /= c1;
+  const uint32_t cz = q % c2; q /= c2;
+  int64_t so = r.src_off + batch * a.src_size;
+  int64_t dof = r.dst_off + batch * a.out_size;
   for (int i = 0; i < r.nouter; ++i) {
-    const int64_t n = r.n[3 + i];
-    const int64_t idx = q % n;
+    const uint32_t n = static_cast<uint32_t>(r.n[3 + i]);
+    const uint32_t idx = q % n;
     q /= n;
-    v.so += idx * r.s[3 + i];
-    v.dof += idx * r.d[3 + i];
+    so += static_cast<int64_t>(idx) * r.s[3 + i];
+    dof += static_cast<int64_t>(idx) * r.d[3 + i];
   }
   const int x0 = cx * r.t[0], y0 = cy * r.t[1], z0 = cz * r.t[2];
-  v.ex = min(r.t[0], r.n[0] - x0);
-  v.ey = min(r.t[1], r.n[1] - y0);
-  v.ez = min(r.t[2], r.n[2] - z0);
-  v.sx = r.s[0]; v.sy = r.s[1]; v.sz = r.s[2];
-  v.dx = r.d[0]; v.dy = r.d[1]; v.dz = r.d[2];
-  v.so += x0 * v.sx + y0 * v.sy + z0 * v.sz;
-  v.dof += x0 * v.dx + y0 * v.dy + z0 * v.dz;
-  v.px = r.t[0] | 1;         // odd pitch: conflict-free column writes
-  v.ty = r.t[1];
-  v.mode = r.mode;
-  v.slot = r.coef_slot;
-  return v;
+  s.ex = min(r.t[0], r.n[0] - x0);
+  s.ey = min(r.t[1], r.n[1] - y0);
+  s.ez = min(r.t[2], r.n[2] - z0);
+  s.so = so + x0 * r.s[0] + y0 * r.s[1] + z0 * r.s[2];
+  s.dof = dof + x0 * r.d[0] + y0 * r.d[1] + z0 * r.d[2];
+  s.sx = static_cast<Off>(r.s[0]); s.sy = static_cast<Off>(r.s[1]); s.sz = static_cast<Off>(r.s[2]);
+  s.dx = static_cast<Off>(r.d[0]); s.dy = static_cast<Off>(r.d[1]); s.dz = static_cast<Off>(r.d[2]);
+  s.px = r.t[0] | 1;
+  s.pz = s.px * r.t[1];
+  s.mode = r.mode;
+  s.slot = r.coef_slot;
+  s.batch = batch;
 }
 
-// Walk `rows` rows of `len` elements: whole warps per row for long rows,
-// several rows per warp for short ones.  f(row, col).
-template <typename F>
-__device__ __forceinline__ void ForRows(int rows, int len, F&& f) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (len > 16) {
-    for (int r = warp; r < rows; r += kWarps) {
-#pragma unroll 2
-      for (int c = lane; c < len; c += 32) f(r, c);
-    }
-  } else {
-    const int per = 32 / len;
-    const int sub = lane / len;
-    const int col = lane - sub * len;
-    if (sub >= per) return;
-#pragma unroll 4
-    for (int r = warp * per + sub; r < rows; r += kWarps * per) f(r, col);
-  }
-}
-
-// Per-operation element function applied when a value reaches the destination.
+// Per-operation element rule applied when a value reaches the destination.
 template <int Op, typename T, typename CA, typename CB>
 struct Emit;
 
 // Copy: bit-preserving move (T is an unsigned storage type).
 template <typename T, typename CA, typename CB>
 struct Emit<kOpCopy, T, CA, CB> {
+  static constexpr bool kReadsBase = false;
   __device__ __forceinline__ Emit(const MapArgs&, int, int64_t) {}
   __device__ __forceinline__ bool SkipSource() const { return false; }
-  __device__ __forceinline__ T operator()(T v, const T*, int64_t) const { return v; }
+  __device__ __forceinline__ bool NeedsBase() const { return false; }
+  __device__ __forceinline__ T operator()(T v, T) const { return v; }
 };
 
-// Accumulation into a zeroed output: 0 + c * v, with the zero/one rules.
+// Accumulation into a zeroed output: 0 + c * v, with the zero / one rules.
 template <typename T, typename CA, typename CB>
 struct Emit<kOpAccumulation, T, CA, CB> {
+  static constexpr bool kReadsBase = false;
   using Real = typename Elem<T>::Real;
   using C = typename BoundOf<Real, CA>::type;
   C c;
@@ -135,7 +126,8 @@ struct Emit<kOpAccumulation, T, CA, CB> {
     }
   }
   __device__ __forceinline__ bool SkipSource() const { return zero; }
-  __device__ __forceinline__ T operator()(T v, const T*, int64_t) const {
+  __device__ __forceinline__ bool NeedsBase() const { return false; }
+  __device__ __forceinline__ T operator()(T v, T) const {
     if (zero) return Zero<T>();
     return PlusZero(one ? v : Scale(c, v));
   }
@@ -144,6 +136,7 @@ struct Emit<kOpAccumulation, T, CA, CB> {
 // Update: alpha * src + beta * base with the reference's short-circuits.
 template <typename T, typename CA, typename CB>
 struct Emit<kOpUpdate, T, CA, CB> {
+  static constexpr bool kReadsBase = true;
   using Real = typename Elem<T>::Real;
   using A = typename BoundOf<Real, CA>::type;
   using B = typename BoundOf<Real, CB>::type;
@@ -155,62 +148,115 @@ struct Emit<kOpUpdate, T, CA, CB> {
     a0 = IsZero(a); a1 = IsOne(a); b0 = IsZero(b); b1 = IsOne(b);
   }
   __device__ __forceinline__ bool SkipSource() const { return a0; }
-  __device__ __forceinline__ T operator()(T v, const T* base, int64_t at) const {
+  __device__ __forceinline__ bool NeedsBase() const { return !b0; }
+  __device__ __forceinline__ T operator()(T v, T old) const {
     if (a0) {
       if (b0) return Zero<T>();
-      const T old = base[at];
       return b1 ? old : Scale(b, old);
     }
     const T s = a1 ? v : Scale(a, v);
     if (b0) return s;
-    const T old = base[at];
     return Add(s, b1 ? old : Scale(b, old));
   }
 };
 
-template <int Op, typename T, typename CA, typename CB>
-__global__ void __launch_bounds__(kThreads) MapKernel(MapArgs args) {
+// Walk `rows` rows of `len` (1..64) elements.  Rows longer than 16 take a
+// whole warp (one lane per column, two column chunks at most); shorter rows
+// are packed several to a warp.  Each warp steps through kUnroll rows at a
+// time so loads of different rows are in flight together.  f(row, column).
+template <typename F>
+__device__ __forceinline__ void WalkRows(int rows, int len, F&& f) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (len > 16) {
+    for (int r0 = warp; r0 < rows; r0 += kWarps * kUnroll) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int r = r0 + u * kWarps;
+        if (r < rows) {
+          if (lane < len) f(r, lane);
+          if (lane + 32 < len) f(r, lane + 32);
+        }
+      }
+    }
+  } else {
+    const int per = 32 / len;
+    const int sub = lane / len;
+    if (sub >= per) return;
+    const int col = lane - sub * len;
+    for (int r0 = warp * per + sub; r0 < rows; r0 += kWarps * per * kUnroll) {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int r = r0 + u * kWarps * per;
+        if (r < rows) f(r, col);
+      }
+    }
+  }
+}
+
+template <int Op, typename T, typename CA, typename CB, typename Off>
+__global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ TileState<Off> st;
   T* tile = reinterpret_cast<T*>(smem_raw);
-  const T* __restrict__ src = static_cast<const T*>(args.src);
-  const T* base = static_cast<const T*>(args.base);
-  T* out = static_cast<T*>(args.out);
   const int64_t total = args.tiles_per_batch * args.batches;
-  for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
-    const int64_t batch = t / args.tiles_per_batch;
-    const int64_t local = t - batch * args.tiles_per_batch;
-    const MapRecord& rec = args.recs[FindRecord(args.recs, args.nrec, local)];
-    const TileView v = DecodeTile(rec, local, batch, args.src_size, args.out_size);
-    const Emit<Op, T, CA, CB> emit(args, v.slot, batch);
+  const int64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * per_cta;
+  const int64_t last = min(total, first + per_cta);
+  int64_t cursor = -1;   // record cursor, meaningful in thread 0 only
+  for (int64_t t = first; t < last; ++t) {
+    if (threadIdx.x == 0) DecodeTile<Off>(args, t, cursor, st);
+    __syncthreads();
+    const Emit<Op, T, CA, CB> emit(args, st.slot, st.batch);
+    const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
+    const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
+    T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
     const bool skip = emit.SkipSource();
-    if (v.mode == kDirect || skip) {
-      // Rows along X; with a skipped source only the destination side is touched.
-      const int rows = v.ey * v.ez;
-      ForRows(rows, v.ex, [&](int r, int x) {
-        const int z = r / v.ey;
-        const int y = r - z * v.ey;
-        const int64_t at = v.dof + x * v.dx + y * v.dy + z * v.dz;
-        T value{};
-        if (!skip) value = src[v.so + x * v.sx + y * v.sy + z * v.sz];
-        out[at] = emit(value, base, at);
+    const bool needs_base = emit.NeedsBase();
+    const int ex = st.ex, ey = st.ey, ez = st.ez;
+    if (st.mode == kDirect || skip) {
+      // Rows along X, one per (y, z); a skipped source touches only the destination.
+      const Off sx = st.sx, sy = st.sy, sz = st.sz, dx = st.dx, dy = st.dy, dz = st.dz;
+      const FastDiv by_ey(static_cast<uint32_t>(ey));
+      WalkRows(ey * ez, ex, [&](int r, int x) {
+        const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
+        const int y = r - z * ey;
+        const Off at = y * dy + z * dz + x * dx;
+        T v{}, old{};
+        if (!skip) v = src[y * sy + z * sz + x * sx];
+        if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+          if (needs_base) old = base[at];
+        }
+        out[at] = emit(v, old);
       });
     } else {
-      // Load: rows along Y, one per (x, z).
-      const FastDiv by_ex(static_cast<uint32_t>(v.ex));
-      ForRows(v.ex * v.ez, v.ey, [&](int r, int y) {
-        const int z = static_cast<int>(by_ex.Div(static_cast<uint32_t>(r)));
-        const int x = r - z * v.ex;
-        tile[x + v.px * (y + v.ty * z)] = src[v.so + x * v.sx + y * v.sy + z * v.sz];
-      });
+      // Load: rows along Y, one per (x, z), into tile[x + px * y + pz * z].
+      {
+        const Off sx = st.sx, sy = st.sy, sz = st.sz;
+        const int px = st.px, pz = st.pz;
+        const FastDiv by_ex(static_cast<uint32_t>(ex));
+        WalkRows(ex * ez, ey, [&](int r, int y) {
+          const int z = static_cast<int>(by_ex.Div(static_cast<uint32_t>(r)));
+          const int x = r - z * ex;
+          tile[x + pz * z + px * y] = src[x * sx + z * sz + y * sy];
+        });
+      }
       __syncthreads();
       // Store: rows along X, one per (y, z).
-      const FastDiv by_ey(static_cast<uint32_t>(v.ey));
-      ForRows(v.ey * v.ez, v.ex, [&](int r, int x) {
-        const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
-        const int y = r - z * v.ey;
-        const int64_t at = v.dof + x * v.dx + y * v.dy + z * v.dz;
-        out[at] = emit(tile[x + v.px * (y + v.ty * z)], base, at);
-      });
+      {
+        const Off dx = st.dx, dy = st.dy, dz = st.dz;
+        const int px = st.px, pz = st.pz;
+        const FastDiv by_ey(static_cast<uint32_t>(ey));
+        WalkRows(ey * ez, ex, [&](int r, int x) {
+          const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
+          const int y = r - z * ey;
+          const Off at = y * dy + z * dz + x * dx;
+          T old{};
+          if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+            if (needs_base) old = base[at];
+          }
+          out[at] = emit(tile[px * y + pz * z + x], old);
+        });
+      }
     }
     __syncthreads();
   }
@@ -264,7 +310,6 @@ __global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
     const int64_t local = task - g.task_begin;
     const int64_t chunk = local / g.owners;
     const int64_t owner = local - chunk * g.owners;
-    // Owner coordinates (map axes, innermost first).
     int idx[kMaxRank];
     int64_t rem = owner;
     for (int a = 0; a < g.rank; ++a) { idx[a] = static_cast<int>(rem % g.n[a]); rem /= g.n[a]; }
@@ -345,21 +390,27 @@ int SmCount() {
   return count;
 }
 
-template <int Op, typename T, typename CA, typename CB>
-void LaunchMapTyped(const MapArgs& args, int smem, cudaStream_t stream) {
-  auto kernel = MapKernel<Op, T, CA, CB>;
-  static bool configured = false;
-  if (!configured) {
-    Check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024), "map attribute");
-    configured = true;
-  }
+template <int Op, typename T, typename CA, typename CB, typename Off>
+void LaunchMapKernel(const MapArgs& args, int smem, cudaStream_t stream) {
+  auto kernel = MapKernel<Op, T, CA, CB, Off>;
+  static int per_sm = [&] {
+    Check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024), "map attribute");
+    return 0;
+  }();
+  int blocks = 0;
+  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, smem), "map occupancy");
+  per_sm = std::max(blocks, 1);
   const int64_t total = args.tiles_per_batch * args.batches;
-  int per_sm = 0;
-  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem), "map occupancy");
-  const int64_t grid = std::min<int64_t>(total, static_cast<int64_t>(std::max(per_sm, 1)) * SmCount());
+  const int64_t grid = std::min<int64_t>(total, static_cast<int64_t>(per_sm) * SmCount());
   kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
   Check(cudaGetLastError(), "map launch");
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+template <int Op, typename T, typename CA, typename CB>
+void LaunchMapTyped(const MapArgs& args, int smem, bool wide, cudaStream_t stream) {
+  if (wide) LaunchMapKernel<Op, T, CA, CB, int64_t>(args, smem, stream);
+  else LaunchMapKernel<Op, T, CA, CB, int32_t>(args, smem, stream);
 }
 
 template <typename Real, typename Complex, typename F>
@@ -374,7 +425,7 @@ void VisitCoefficient(int32_t dtype, bool complex_storage, F&& f) {
   throw InvalidArgumentError("unsupported CUDA coefficient dtype; expected S32 or matching real/complex precision");
 }
 
-template <typename T, typename F>
+template <typename F>
 void WithStorage(int32_t dtype, F&& f) {
   switch (dtype) {
     case 11: f(static_cast<float*>(nullptr)); return;
@@ -387,6 +438,10 @@ void WithStorage(int32_t dtype, F&& f) {
 
 }  // namespace
 
+void Check(cudaError_t status, const char* what) {
+  if (status != cudaSuccess) throw std::runtime_error(std::string("CUDA ") + what + ": " + cudaGetErrorString(status));
+}
+
 int MapSharedBytes(const MapRecord* recs, int64_t count, int element_bytes) {
   int64_t best = 0;
   for (int64_t i = 0; i < count; ++i) {
@@ -397,21 +452,21 @@ int MapSharedBytes(const MapRecord* recs, int64_t count, int element_bytes) {
 }
 
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
-               int smem, cudaStream_t stream) {
-  WithStorage<void>(dtype, [&](auto* tag) {
+               int smem, bool wide, cudaStream_t stream) {
+  WithStorage(dtype, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
     using Real = typename Elem<T>::Real;
     using Complex = std::conditional_t<sizeof(Real) == 4, float2, double2>;
     constexpr bool kComplex = Elem<T>::kComplex;
     if (op == kOpCopy) {
       using Bits = std::conditional_t<sizeof(T) == 4, uint32_t, std::conditional_t<sizeof(T) == 8, uint2, uint4>>;
-      LaunchMapTyped<kOpCopy, Bits, int32_t, int32_t>(args, smem, stream);
+      LaunchMapTyped<kOpCopy, Bits, int32_t, int32_t>(args, smem, wide, stream);
     } else if (op == kOpAccumulation) {
       VisitCoefficient<Real, Complex>(ca_dtype, kComplex, [&](auto* ca) {
         using CA = std::remove_cv_t<std::remove_pointer_t<decltype(ca)>>;
         if constexpr (!kComplex && sizeof(CA) == 2 * sizeof(Real)) {
         } else {
-          LaunchMapTyped<kOpAccumulation, T, CA, int32_t>(args, smem, stream);
+          LaunchMapTyped<kOpAccumulation, T, CA, int32_t>(args, smem, wide, stream);
         }
       });
     } else {
@@ -421,7 +476,7 @@ void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const 
           using CB = std::remove_cv_t<std::remove_pointer_t<decltype(cb)>>;
           if constexpr (!kComplex && (sizeof(CA) == 2 * sizeof(Real) || sizeof(CB) == 2 * sizeof(Real))) {
           } else {
-            LaunchMapTyped<kOpUpdate, T, CA, CB>(args, smem, stream);
+            LaunchMapTyped<kOpUpdate, T, CA, CB>(args, smem, wide, stream);
           }
         });
       });
@@ -430,7 +485,7 @@ void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const 
 }
 
 void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream) {
-  WithStorage<void>(dtype, [&](auto* tag) {
+  WithStorage(dtype, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
     using Real = typename Elem<T>::Real;
     using Complex = std::conditional_t<sizeof(Real) == 4, float2, double2>;

@@ -57,7 +57,7 @@ void Check(cudaError_t status, const char* what);
 
 int MapSharedBytes(const MapRecord* recs, int64_t count, int element_bytes);
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
-               int smem, cudaStream_t stream);
+               int smem, bool wide, cudaStream_t stream);
 void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream);
 void LaunchAxpby(int32_t dtype, int64_t n, double ar, double ai, const void* x, double br, double bi,
                  const void* y, void* out, cudaStream_t stream);

@@ -157,7 +157,7 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_byte
   if (!rest.empty()) { z_axis = rest.front(); rest.erase(rest.begin()); }
   if (x == y) {
     out.mode = kDirect;
-    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], budget));
+    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], 64));   // rows of at most 64 (two lanes' worth)
     out.t[1] = 1;
   } else {
     out.mode = kTranspose;
@@ -176,7 +176,25 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_byte
 int64_t MapTiles(const MapRecord& record) {
   int64_t tiles = int64_t{record.c[0]} * record.c[1] * record.c[2];
   for (int i = 0; i < record.nouter; ++i) tiles *= record.n[3 + i];
+  if (tiles >= (int64_t{1} << 31)) {
+    throw std::runtime_error("a record spans more than 2^31 tiles; split it into smaller records");
+  }
   return tiles;
+}
+
+// In-tile offsets fit in int32 when every box-axis stride and span does.
+bool NeedsWideOffsets(const MapRecord& record) {
+  constexpr int64_t kLimit = (int64_t{1} << 31) - 1;
+  int64_t src_span = 0, dst_span = 0;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t s = record.s[i] < 0 ? -record.s[i] : record.s[i];
+    const int64_t d = record.d[i] < 0 ? -record.d[i] : record.d[i];
+    if (s > kLimit || d > kLimit) return true;
+    src_span += (record.t[i] - 1) * s;
+    dst_span += (record.t[i] - 1) * d;
+    if (src_span > kLimit || dst_span > kLimit) return true;
+  }
+  return false;
 }
 
 template <typename T>
@@ -305,6 +323,7 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     Canonicalize(fused, true);
     MapRecord record = MakeMapRecord(fused, record_slot[i], element_bytes, tiles);
     tiles += MapTiles(record);
+    plan.map_wide = plan.map_wide || NeedsWideOffsets(record);
     covered += ElementCount(records[i]);
     read_elements += ElementCount(records[i]);
     map_records.push_back(record);

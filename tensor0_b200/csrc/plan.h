@@ -105,6 +105,7 @@ struct Plan {
   bool full_coverage = false;    // the map engine writes every output element
   bool has_map = false;
   bool has_reduce = false;
+  bool map_wide = false;         // some tile needs 64-bit in-tile offsets
   uint64_t map_tiles = 0;
   uint64_t tasks = 0;
   uint64_t owners = 0;

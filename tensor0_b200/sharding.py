@@ -1,0 +1,112 @@
+"""Sector (record) sharding across GPUs with longest-processing-time balancing.
+
+Charge sectors are independent: every record of a permute reads one source
+sub-block and writes one destination sub-block.  A shard owns a set of
+records, holds their source sub-blocks compacted in its own HBM (input
+sharding by record) and writes their destination sub-blocks compacted, so the
+timed kernels need no communication.  Collectives are used only to gather (or
+reshard) outputs whose ownership changes, outside the kernels' timed region.
+"""
+
+from __future__ import annotations
+
+import heapq
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import stride
+
+
+def lpt_partition(costs, parts: int) -> list[np.ndarray]:
+    """Greedy LPT: largest cost first, each to the least-loaded part (ties to
+    the lowest part index).  Deterministic; returns sorted index arrays."""
+    costs = np.asarray(costs, dtype=np.float64)
+    if parts < 1:
+        raise ValueError("parts must be positive")
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    heap = [(0.0, p) for p in range(parts)]
+    owned: list[list[int]] = [[] for _ in range(parts)]
+    for i in order:
+        load, p = heapq.heappop(heap)
+        owned[p].append(i)
+        heapq.heappush(heap, (load + costs[i], p))
+    return [np.array(sorted(o), dtype=np.int64) for o in owned]
+
+
+def _row_major(shape: np.ndarray) -> np.ndarray:
+    strides = np.ones_like(shape)
+    for axis in range(shape.shape[1] - 2, -1, -1):
+        strides[:, axis] = strides[:, axis + 1] * shape[:, axis + 1]
+    return strides
+
+
+@dataclass
+class PermuteShard:
+    """One rank's part of a permute: owned records and their compacted layout."""
+
+    rank: int
+    world: int
+    records: np.ndarray          # global record indices (ascending)
+    src_sizes: np.ndarray        # [R, rank] source sub-block sizes (source axis order)
+    src_strides: np.ndarray      # [R, rank] global source strides
+    src_offsets: np.ndarray      # [R] global source offsets
+    dst_sizes: np.ndarray        # [R, rank] destination sub-block sizes
+    dst_strides: np.ndarray      # [R, rank] global destination strides
+    dst_offsets: np.ndarray      # [R] global destination offsets
+    local_src_offsets: np.ndarray
+    local_dst_offsets: np.ndarray
+    local_source_size: int
+    local_output_size: int
+    words: np.ndarray            # local layout words
+
+    @property
+    def bytes_per_element_pair(self) -> int:
+        return int(np.prod(self.dst_sizes, axis=1).sum())
+
+    def _addresses(self, sizes, strides, offset):
+        index = np.full(tuple(sizes), offset, dtype=np.int64)
+        for axis, (n, s) in enumerate(zip(sizes, strides)):
+            view = [1] * len(sizes)
+            view[axis] = n
+            index = index + np.arange(n, dtype=np.int64).reshape(view) * s
+        return index.reshape(-1)
+
+    def source_index(self) -> np.ndarray:
+        """Global source address of every local source element, in local order."""
+        parts = [self._addresses(s, t, o) for s, t, o in zip(self.src_sizes, self.src_strides, self.src_offsets)]
+        return np.concatenate(parts) if parts else np.zeros(0, np.int64)
+
+    def output_index(self) -> np.ndarray:
+        """Global destination address of every local output element, in local order."""
+        parts = [self._addresses(s, t, o) for s, t, o in zip(self.dst_sizes, self.dst_strides, self.dst_offsets)]
+        return np.concatenate(parts) if parts else np.zeros(0, np.int64)
+
+
+def shard_permute(plan, rank: int, world: int, element_bytes: int = 8) -> PermuteShard:
+    """LPT-partition a permute's records (cost = bytes moved) and build the
+    compacted local layout of shard ``rank``."""
+    from .structure import degeneracy_structure
+
+    sd = degeneracy_structure(plan.src)
+    counts = np.prod(plan.shape, axis=1) if plan.shape.size else np.ones(len(plan.transform.src), np.int64)
+    owned = lpt_partition(2 * counts * element_bytes, world)[rank]
+    src_idx = plan.transform.src[owned]
+    src_sizes = sd.sizes[src_idx]
+    src_strides = sd.strides[src_idx]
+    dst_sizes = plan.shape[owned]
+    local_counts = np.prod(dst_sizes, axis=1) if len(owned) else np.zeros(0, np.int64)
+    local_offsets = np.concatenate([[0], np.cumsum(local_counts)[:-1]]).astype(np.int64) if len(owned) else \
+        np.zeros(0, np.int64)
+    total = int(local_counts.sum())
+    # Local source sub-blocks are compact row-major in source axis order; the
+    # record reads them through the permutation.
+    perm = list(plan.perm)
+    compact_src = _row_major(src_sizes) if len(owned) else np.zeros((0, src_sizes.shape[1]), np.int64)
+    local_src_strides = compact_src[:, perm] if len(owned) else compact_src
+    local_dst_strides = _row_major(dst_sizes) if len(owned) else np.zeros_like(dst_sizes)
+    words = stride.encode_layout_arrays(dst_sizes, local_src_strides, local_offsets, local_dst_strides,
+                                        local_offsets, source_size=total, output_size=total)
+    return PermuteShard(rank, world, owned, src_sizes, src_strides, sd.offsets[src_idx], dst_sizes,
+                        plan.dst_strides[owned], plan.dst_offsets[owned], local_offsets, local_offsets, total, total,
+                        words)

@@ -126,6 +126,7 @@ class PermutePlan:
     src_offsets: np.ndarray
     dst_strides: np.ndarray
     dst_offsets: np.ndarray
+    perm: tuple = ()
     _plans: dict = None
 
     @property
@@ -164,7 +165,7 @@ def permute_plan(src: HomSpace, p_codomain: tuple[int, ...], p_domain: tuple[int
                                         dd.offsets[transform.dst], source_size=sd.total_dim,
                                         output_size=dd.total_dim)
     return PermutePlan(src, dst, words, transform, bool(disjoint), shape, sstr, sd.offsets[transform.src],
-                       dd.strides[transform.dst], dd.offsets[transform.dst])
+                       dd.strides[transform.dst], dd.offsets[transform.dst], tuple(perm))
 
 
 def _normalize_p(space: HomSpace, p) -> tuple[tuple[int, ...], tuple[int, ...]]:

@@ -93,6 +93,8 @@ def random_layout(rng, source_size, output_size, records, max_rank=4, max_extent
         count = int(np.prod(shape))
         if cursor + count > output_size:
             break
+        if count > source_size:
+            continue
         dst = stride.contiguous_strides(shape)
         perm = rng.permutation(rank)
         src_shape = tuple(shape[p] for p in perm)
