@@ -28,13 +28,17 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 4;   // rows per warp step
 
-// Division by a runtime divisor in [1, 2^24) for dividends below 2^24.
+// Division by a runtime divisor in [1, 2^24) for dividends below 2^24:
+// n / d = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1 (round-up multiplier method).
 struct FastDiv {
   uint32_t m, l;
-  __device__ __forceinline__ explicit FastDiv(uint32_t divisor) {
-    l = 32 - __clz(divisor - 1);                         // ceil(log2(divisor))
+  __device__ __forceinline__ FastDiv() = default;
+  __device__ __forceinline__ FastDiv(uint32_t magic, uint32_t shift) : m(magic), l(shift) {}
+  __device__ __forceinline__ static FastDiv Of(uint32_t divisor) {
+    const uint32_t shift = 32 - __clz(divisor - 1);
     const uint64_t one = 1;
-    m = static_cast<uint32_t>(((one << 32) * ((one << l) - divisor)) / divisor + 1);
+    return FastDiv(static_cast<uint32_t>(((one << 32) * ((one << shift) - divisor)) / divisor + 1), shift);
   }
   __device__ __forceinline__ uint32_t Div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
 };
@@ -48,6 +52,8 @@ struct TileState {
   int ex, ey, ez;         // tile extents (edge tiles are smaller)
   int px, pz;             // shared-memory pitches: along Y (odd, >= ex) and along Z
   int mode, slot;
+  int per_x, per_y;       // rows of ex (ey) elements packed per warp when short
+  FastDiv div_x, div_y;   // division by ex and by ey
   int64_t batch;
 };
 
@@ -92,6 +98,10 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64
   s.pz = s.px * r.t[1];
   s.mode = r.mode;
   s.slot = r.coef_slot;
+  s.per_x = s.ex <= 16 ? 32 / s.ex : 1;
+  s.per_y = s.ey <= 16 ? 32 / s.ey : 1;
+  s.div_x = FastDiv::Of(static_cast<uint32_t>(s.ex));
+  s.div_y = FastDiv::Of(static_cast<uint32_t>(s.ey));
   s.batch = batch;
 }
 
@@ -165,7 +175,7 @@ struct Emit<kOpUpdate, T, CA, CB> {
 // are packed several to a warp.  Each warp steps through kUnroll rows at a
 // time so loads of different rows are in flight together.  f(row, column).
 template <typename F>
-__device__ __forceinline__ void WalkRows(int rows, int len, F&& f) {
+__device__ __forceinline__ void WalkRows(int rows, int len, int per, FastDiv by_len, F&& f) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (len > 16) {
     for (int r0 = warp; r0 < rows; r0 += kWarps * kUnroll) {
@@ -179,8 +189,7 @@ __device__ __forceinline__ void WalkRows(int rows, int len, F&& f) {
       }
     }
   } else {
-    const int per = 32 / len;
-    const int sub = lane / len;
+    const int sub = static_cast<int>(by_len.Div(static_cast<uint32_t>(lane)));
     if (sub >= per) return;
     const int col = lane - sub * len;
     for (int r0 = warp * per + sub; r0 < rows; r0 += kWarps * per * kUnroll) {
@@ -216,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
     if (st.mode == kDirect || skip) {
       // Rows along X, one per (y, z); a skipped source touches only the destination.
       const Off sx = st.sx, sy = st.sy, sz = st.sz, dx = st.dx, dy = st.dy, dz = st.dz;
-      const FastDiv by_ey(static_cast<uint32_t>(ey));
-      WalkRows(ey * ez, ex, [&](int r, int x) {
+      const FastDiv by_ey = st.div_y;
+      WalkRows(ey * ez, ex, st.per_x, st.div_x, [&](int r, int x) {
         const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
         const int y = r - z * ey;
         const Off at = y * dy + z * dz + x * dx;
@@ -233,8 +242,8 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
       {
         const Off sx = st.sx, sy = st.sy, sz = st.sz;
         const int px = st.px, pz = st.pz;
-        const FastDiv by_ex(static_cast<uint32_t>(ex));
-        WalkRows(ex * ez, ey, [&](int r, int y) {
+        const FastDiv by_ex = st.div_x;
+        WalkRows(ex * ez, ey, st.per_y, st.div_y, [&](int r, int y) {
           const int z = static_cast<int>(by_ex.Div(static_cast<uint32_t>(r)));
           const int x = r - z * ex;
           tile[x + pz * z + px * y] = src[x * sx + z * sz + y * sy];
@@ -245,8 +254,8 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
       {
         const Off dx = st.dx, dy = st.dy, dz = st.dz;
         const int px = st.px, pz = st.pz;
-        const FastDiv by_ey(static_cast<uint32_t>(ey));
-        WalkRows(ey * ez, ex, [&](int r, int x) {
+        const FastDiv by_ey = st.div_y;
+        WalkRows(ey * ez, ex, st.per_x, st.div_x, [&](int r, int x) {
           const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
           const int y = r - z * ey;
           const Off at = y * dy + z * dz + x * dx;

@@ -18,7 +18,7 @@ constexpr uint64_t kExtentLimit = uint64_t{1} << 30;   // per-axis extent kept i
 constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap check
 
 // Bytes of shared memory one map tile may stage (before row padding).
-constexpr int64_t kTileBytes = 16384;
+constexpr int64_t kTileBytes = 32768;
 
 // Split records so every axis extent fits in int32 and at most kMaxRank axes remain.
 std::vector<Record> SplitForDevice(const Record& record) {
@@ -153,8 +153,35 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_byte
     return out;
   }
   put(0, x);
+  // The third box axis extends whichever contiguous run the box leaves
+  // shorter: the destination run (X, possibly continued by Y) or the source
+  // run (Y).  Short source runs waste DRAM bursts: the bytes that follow a run
+  // belong to a later tile and are evicted before it runs.
   std::size_t z_axis = rank;
-  if (!rest.empty()) { z_axis = rest.front(); rest.erase(rest.begin()); }
+  if (!rest.empty()) {
+    const uint64_t nx = record.shape[x], ny = record.shape[y];
+    const bool y_continues_dst = x != y && record.dstr[y] == static_cast<int64_t>(nx) * record.dstr[x];
+    const uint64_t dst_run = x == y ? nx : (y_continues_dst ? nx * ny : nx);
+    const uint64_t src_run = x == y ? nx : ny;
+    auto continues = [&](std::size_t axis, bool source) {
+      const std::size_t from = source ? y : (y_continues_dst ? y : x);
+      const auto& strides = source ? record.sstr : record.dstr;
+      return strides[axis] == static_cast<int64_t>(record.shape[from]) * strides[from];
+    };
+    std::size_t pick = rest.front();
+    bool found = false;
+    const bool extend_source = src_run <= dst_run;
+    for (std::size_t axis : rest) {
+      if (continues(axis, extend_source)) { pick = axis; found = true; break; }
+    }
+    if (!found) {
+      for (std::size_t axis : rest) {
+        if (continues(axis, !extend_source)) { pick = axis; break; }
+      }
+    }
+    z_axis = pick;
+    rest.erase(std::find(rest.begin(), rest.end(), pick));
+  }
   if (x == y) {
     out.mode = kDirect;
     out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], 64));   // rows of at most 64 (two lanes' worth)

@@ -279,9 +279,12 @@ def execute_update(source: torch.Tensor, base: torch.Tensor, alpha, beta, plan: 
     real = torch.float32 if base.dtype in (torch.float32, torch.complex64) else torch.float64
 
     def coefficient(value):
-        tensor = value if isinstance(value, torch.Tensor) else torch.as_tensor(value)
-        if tensor.dtype not in _COEFFICIENT:
-            tensor = tensor.to(real)
+        if isinstance(value, torch.Tensor):
+            tensor = value if value.dtype in _COEFFICIENT else value.to(real)
+        elif isinstance(value, complex) and value.imag != 0:
+            tensor = torch.tensor([value], dtype=base.dtype)
+        else:
+            tensor = torch.tensor([complex(value).real if isinstance(value, complex) else value], dtype=real)
         if tensor.is_complex() and not base.is_complex():
             raise ValueError("unsupported CUDA coefficient dtype; expected S32 or matching real/complex precision")
         tensor = tensor.to(base.device).reshape(-1).contiguous()
