@@ -5,12 +5,12 @@
 // every batch; each CTA walks a contiguous range of tiles.  A tile is a box
 // over the record's destination-innermost axis X, its source-innermost axis Y
 // and one further axis Z.  One thread decodes the tile (record cursor, chunk
-// coordinates, outer axes) into shared memory; then the CTA reads the tile
-// with lanes running along Y (coalesced source reads), stages it in shared
-// memory and writes it with lanes running along X (coalesced destination
-// writes).  When X and Y coincide the tile is copied row by row.  Rows are
-// handled several at a time per warp so each thread keeps several loads in
-// flight before it stores.
+// coordinates, outer axes) into shared memory.  The CTA then copies the tile
+// in contiguous runs: source runs (Y, continued by Z when Z follows Y in the
+// source) into shared memory, and destination runs (X, continued by Y when Y
+// follows X in the destination) out of it.  Lanes stride each run, so reads
+// and writes are coalesced and each element costs a few integer operations.
+// When X and Y coincide the tile is copied run by run without staging.
 #include "engine.h"
 
 #include "arith.cuh"
@@ -26,7 +26,6 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 4;   // rows per warp step
 
 // Division by a runtime divisor in [1, 2^24) for dividends below 2^24:
 // n / d = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
@@ -50,10 +49,12 @@ struct TileState {
   int64_t so, dof;        // element offsets of the tile origin, batch included
   Off sx, sy, sz, dx, dy, dz;
   int ex, ey, ez;         // tile extents (edge tiles are smaller)
-  int px, pz;             // shared-memory pitches: along Y (odd, >= ex) and along Z
+  int px, pz;             // shared-memory pitches along Y (odd, >= ex) and Z
   int mode, slot;
-  int per_x, per_y;       // rows of ex (ey) elements packed per warp when short
-  FastDiv div_x, div_y;   // division by ex and by ey
+  int src_runs, src_len;  // source runs: ex runs of ey*ez (Z follows Y) or ex*ez runs of ey
+  int dst_runs, dst_len;  // destination runs: ez runs of ex*ey (Y follows X) or ey*ez runs of ex
+  int src_linear, dst_linear;
+  FastDiv div_x, div_y, div_src, div_dst;   // by ex, by ey, by src_len, by dst_len
   int64_t batch;
 };
 
@@ -87,9 +88,10 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64
     dof += static_cast<int64_t>(idx) * r.d[3 + i];
   }
   const int x0 = cx * r.t[0], y0 = cy * r.t[1], z0 = cz * r.t[2];
-  s.ex = min(r.t[0], r.n[0] - x0);
-  s.ey = min(r.t[1], r.n[1] - y0);
-  s.ez = min(r.t[2], r.n[2] - z0);
+  const int ex = min(r.t[0], r.n[0] - x0);
+  const int ey = min(r.t[1], r.n[1] - y0);
+  const int ez = min(r.t[2], r.n[2] - z0);
+  s.ex = ex; s.ey = ey; s.ez = ez;
   s.so = so + x0 * r.s[0] + y0 * r.s[1] + z0 * r.s[2];
   s.dof = dof + x0 * r.d[0] + y0 * r.d[1] + z0 * r.d[2];
   s.sx = static_cast<Off>(r.s[0]); s.sy = static_cast<Off>(r.s[1]); s.sz = static_cast<Off>(r.s[2]);
@@ -98,10 +100,23 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64
   s.pz = s.px * r.t[1];
   s.mode = r.mode;
   s.slot = r.coef_slot;
-  s.per_x = s.ex <= 16 ? 32 / s.ex : 1;
-  s.per_y = s.ey <= 16 ? 32 / s.ey : 1;
-  s.div_x = FastDiv::Of(static_cast<uint32_t>(s.ex));
-  s.div_y = FastDiv::Of(static_cast<uint32_t>(s.ey));
+  // Z continues the source run of Y when sz = ey * sy and the shared-memory
+  // Z pitch equals px * ey (a full-height tile); Y continues the destination
+  // run of X when dy = ex * dx.
+  s.src_linear = ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ey == r.t[1];
+  s.dst_linear = ey > 1 && r.d[1] == static_cast<int64_t>(ex) * r.d[0];
+  if (r.mode == kDirect) {
+    s.src_linear = 0;
+    s.dst_linear = 0;
+  }
+  s.src_runs = s.src_linear ? ex : ex * ez;
+  s.src_len = s.src_linear ? ey * ez : ey;
+  s.dst_runs = s.dst_linear ? ez : ey * ez;
+  s.dst_len = s.dst_linear ? ex * ey : ex;
+  s.div_x = FastDiv::Of(static_cast<uint32_t>(ex));
+  s.div_y = FastDiv::Of(static_cast<uint32_t>(ey));
+  s.div_src = FastDiv::Of(static_cast<uint32_t>(s.src_len));
+  s.div_dst = FastDiv::Of(static_cast<uint32_t>(s.dst_len));
   s.batch = batch;
 }
 
@@ -170,37 +185,37 @@ struct Emit<kOpUpdate, T, CA, CB> {
   }
 };
 
-// Walk `rows` rows of `len` (1..64) elements.  Rows longer than 16 take a
-// whole warp (one lane per column, two column chunks at most); shorter rows
-// are packed several to a warp.  Each warp steps through kUnroll rows at a
-// time so loads of different rows are in flight together.  f(row, column).
-template <typename F>
-__device__ __forceinline__ void WalkRows(int rows, int len, int per, FastDiv by_len, F&& f) {
+// Walk `runs` runs of `len` elements.  Runs of 32 elements or more take a
+// whole warp and lanes stride them (unrolled, so several loads are in flight);
+// shorter runs are packed several to a warp, one element per lane.
+// start(run) -> per-run state; f(state, j) handles element j of the run.
+template <typename StartF, typename F>
+__device__ __forceinline__ void WalkRuns(int runs, int len, FastDiv by_len, StartF&& start, F&& f) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (len > 16) {
-    for (int r0 = warp; r0 < rows; r0 += kWarps * kUnroll) {
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int r = r0 + u * kWarps;
-        if (r < rows) {
-          if (lane < len) f(r, lane);
-          if (lane + 32 < len) f(r, lane + 32);
-        }
-      }
+  if (len >= 32) {
+    for (int r = warp; r < runs; r += kWarps) {
+      const auto state = start(r);
+#pragma unroll 4
+      for (int j = lane; j < len; j += 32) f(state, j);
     }
   } else {
-    const int sub = static_cast<int>(by_len.Div(static_cast<uint32_t>(lane)));
-    if (sub >= per) return;
-    const int col = lane - sub * len;
-    for (int r0 = warp * per + sub; r0 < rows; r0 += kWarps * per * kUnroll) {
+    // Element e of the packed sequence: run e / len, element e % len.
+    const int total = runs * len;
+    for (int e0 = warp * 32; e0 < total; e0 += kThreads * 4) {
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int r = r0 + u * kWarps * per;
-        if (r < rows) f(r, col);
+      for (int u = 0; u < 4; ++u) {
+        const int e = e0 + u * kThreads + lane;
+        if (e < total) {
+          const int r = static_cast<int>(by_len.Div(static_cast<uint32_t>(e)));
+          f(start(r), e - r * len);
+        }
       }
     }
   }
 }
+
+template <typename Off>
+struct Run { Off a, b; int z; };
 
 template <int Op, typename T, typename CA, typename CB, typename Off>
 __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
@@ -221,50 +236,73 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
     T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
     const bool skip = emit.SkipSource();
     const bool needs_base = emit.NeedsBase();
-    const int ex = st.ex, ey = st.ey, ez = st.ez;
+    const int ex = st.ex;
     if (st.mode == kDirect || skip) {
-      // Rows along X, one per (y, z); a skipped source touches only the destination.
+      // Runs along X, one per (y, z); a skipped source touches only the destination.
       const Off sx = st.sx, sy = st.sy, sz = st.sz, dx = st.dx, dy = st.dy, dz = st.dz;
-      const FastDiv by_ey = st.div_y;
-      WalkRows(ey * ez, ex, st.per_x, st.div_x, [&](int r, int x) {
-        const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
-        const int y = r - z * ey;
-        const Off at = y * dy + z * dz + x * dx;
-        T v{}, old{};
-        if (!skip) v = src[y * sy + z * sz + x * sx];
-        if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
-          if (needs_base) old = base[at];
-        }
-        out[at] = emit(v, old);
-      });
+      const int ey = st.ey;
+      const FastDiv by_y = st.div_y;
+      WalkRuns(ey * st.ez, ex, st.div_x,
+          [&](int r) {
+            const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
+            const int y = r - z * ey;
+            return Run<Off>{static_cast<Off>(y * sy + z * sz), static_cast<Off>(y * dy + z * dz), 0};
+          },
+          [&](const Run<Off>& run, int x) {
+            const Off at = run.b + x * dx;
+            T v{}, old{};
+            if (!skip) v = src[run.a + x * sx];
+            if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+              if (needs_base) old = base[at];
+            }
+            out[at] = emit(v, old);
+          });
     } else {
-      // Load: rows along Y, one per (x, z), into tile[x + px * y + pz * z].
+      // Source runs into tile[x + px * y + pz * z].
       {
         const Off sx = st.sx, sy = st.sy, sz = st.sz;
         const int px = st.px, pz = st.pz;
-        const FastDiv by_ex = st.div_x;
-        WalkRows(ex * ez, ey, st.per_y, st.div_y, [&](int r, int y) {
-          const int z = static_cast<int>(by_ex.Div(static_cast<uint32_t>(r)));
-          const int x = r - z * ex;
-          tile[x + pz * z + px * y] = src[x * sx + z * sz + y * sy];
-        });
+        const bool linear = st.src_linear;
+        const FastDiv by_x = st.div_x;
+        WalkRuns(st.src_runs, st.src_len, st.div_src,
+            [&](int r) {
+              if (linear) return Run<Off>{static_cast<Off>(r * sx), static_cast<Off>(r), 0};
+              const int z = static_cast<int>(by_x.Div(static_cast<uint32_t>(r)));
+              const int x = r - z * ex;
+              return Run<Off>{static_cast<Off>(x * sx + z * sz), static_cast<Off>(x + pz * z), 0};
+            },
+            [&](const Run<Off>& run, int j) { tile[run.b + j * px] = src[run.a + j * sy]; });
       }
       __syncthreads();
-      // Store: rows along X, one per (y, z).
+      // Destination runs out of the tile.
       {
         const Off dx = st.dx, dy = st.dy, dz = st.dz;
-        const int px = st.px, pz = st.pz;
-        const FastDiv by_ey = st.div_y;
-        WalkRows(ey * ez, ex, st.per_x, st.div_x, [&](int r, int x) {
-          const int z = static_cast<int>(by_ey.Div(static_cast<uint32_t>(r)));
-          const int y = r - z * ey;
-          const Off at = y * dy + z * dz + x * dx;
-          T old{};
-          if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
-            if (needs_base) old = base[at];
-          }
-          out[at] = emit(tile[px * y + pz * z + x], old);
-        });
+        const int px = st.px, pz = st.pz, ey = st.ey;
+        const bool linear = st.dst_linear;
+        const FastDiv by_x = st.div_x, by_y = st.div_y;
+        WalkRuns(st.dst_runs, st.dst_len, st.div_dst,
+            [&](int r) {
+              if (linear) return Run<Off>{static_cast<Off>(pz * r), static_cast<Off>(r * dz), 0};
+              const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
+              const int y = r - z * ey;
+              return Run<Off>{static_cast<Off>(px * y + pz * z), static_cast<Off>(y * dy + z * dz), 0};
+            },
+            [&](const Run<Off>& run, int k) {
+              // Linear runs cover (x, y) with x fastest: k = x + ex * y.
+              int at_tile;
+              if (linear) {
+                const int y = static_cast<int>(by_x.Div(static_cast<uint32_t>(k)));
+                at_tile = run.a + k + (px - ex) * y;
+              } else {
+                at_tile = run.a + k;
+              }
+              const Off at = run.b + k * dx;
+              T old{};
+              if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+                if (needs_base) old = base[at];
+              }
+              out[at] = emit(tile[at_tile], old);
+            });
       }
     }
     __syncthreads();

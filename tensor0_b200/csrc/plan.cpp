@@ -184,7 +184,7 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_byte
   }
   if (x == y) {
     out.mode = kDirect;
-    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], 64));   // rows of at most 64 (two lanes' worth)
+    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], budget));   // one run per (y, z)
     out.t[1] = 1;
   } else {
     out.mode = kTranspose;
