@@ -142,6 +142,27 @@ int t0b_reduction(const t0b_plan* plan, int32_t dtype, const void* source, void*
                   void* stream, char* error, size_t error_size);
 
 /*
+ * t0b_reduction without a scratch argument, for callers that cannot allocate
+ * device memory (no counterpart in the reference: its reductions receive
+ * XLA-owned scratch).  An XLA FFI handler may not allocate (XLA owns every
+ * buffer), and an application whose device memory is fully reserved by its own
+ * pool cannot call cudaMalloc; both still pass inputs, output, coefficients
+ * and the device table, and the reduce engine's partials go to a 16 MiB array
+ * compiled into this library (held by every GPU that loads it until exit).
+ * Calls needing more than 16 MiB of scratch (batches * scratch elements *
+ * element size) are rejected with status 1.  The first call on a device looks
+ * up the array's device address with that device current; make that first
+ * call before any stream capture.  Every call shares the one array per device:
+ * calls that overlap on the GPU (different streams, no ordering) race.  The
+ * kernels write every partial they read, so nothing needs clearing between
+ * calls.  Allocates nothing.
+ */
+int t0b_reduction_static_scratch(const t0b_plan* plan, int32_t dtype, const void* source, void* output,
+                                 int64_t batches, const void* coefficients, int32_t coefficient_dtype,
+                                 int64_t coefficient_count, const int64_t* device_table, void* stream,
+                                 char* error, size_t error_size);
+
+/*
  * Update (the fused add_transform): out = base; at each selected address
  * out[dst] = alpha * src[src] + beta * base[dst], with the reference's zero
  * and one short-circuits (map_reduce_policies.cuh:30-69).  output may alias

@@ -53,6 +53,10 @@ SIGNATURES = {
                                      ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p,
                                      ctypes.c_size_t]),
+    "t0b_reduction_static_scratch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                                    ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                                    ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
+                                                    ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
     "t0b_update": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
                                   ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                   ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
