@@ -16,7 +16,8 @@
 
 struct t0b_plan {
   t0b::Plan plan;
-  int map_smem = 0;
+  int map_smem = 0;        // dynamic shared memory of one map CTA (bytes)
+  int64_t tile_elems = 0;  // staged-tile elements; update plans place the base buffer after them
 };
 
 namespace {
@@ -117,6 +118,7 @@ void RunMap(const t0b_plan* plan, int op, int32_t dtype, int32_t ca_dtype, int32
   args.out = out;
   args.src_size = static_cast<int64_t>(plan->plan.source_size);
   args.out_size = static_cast<int64_t>(plan->plan.output_size);
+  args.tile_elems = plan->tile_elems;
   args.ca = ca;
   args.ca_count = ca_count;
   args.cb = cb;
@@ -218,9 +220,12 @@ int t0b_plan_create(int32_t operation, const int64_t* words, size_t word_count,
     built->plan = t0b::BuildPlan(operation, words, word_count, coefficient_records, coefficient_count,
                                  element_bytes, flags);
     const auto& h = *reinterpret_cast<const t0b::TableHeader*>(built->plan.table.data());
-    built->map_smem = t0b::MapSharedBytes(
-        reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset), h.map_records,
-        element_bytes);
+    int64_t tile = 0, box = 0;
+    t0b::MapTileElements(reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset),
+                         h.map_records, &tile, &box);
+    // Update plans also stage the destination's base values (one tile box).
+    built->tile_elems = tile;
+    built->map_smem = static_cast<int>((tile + (operation == T0B_OP_UPDATE ? box : 0)) * element_bytes);
     *plan = built.release();
     g_created.fetch_add(1, std::memory_order_relaxed);
   });

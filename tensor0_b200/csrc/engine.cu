@@ -106,11 +106,15 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64
   s.src_linear = ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ey == r.t[1];
   s.dst_linear = ey > 1 && r.d[1] == static_cast<int64_t>(ex) * r.d[0];
   if (r.mode == kDirect) {
+    // Runs along X on both sides, one per (y, z).
     s.src_linear = 0;
     s.dst_linear = 0;
+    s.src_runs = ey * ez;
+    s.src_len = ex;
+  } else {
+    s.src_runs = s.src_linear ? ex : ex * ez;
+    s.src_len = s.src_linear ? ey * ez : ey;
   }
-  s.src_runs = s.src_linear ? ex : ex * ez;
-  s.src_len = s.src_linear ? ey * ez : ey;
   s.dst_runs = s.dst_linear ? ez : ey * ez;
   s.dst_len = s.dst_linear ? ex * ey : ex;
   s.div_x = FastDiv::Of(static_cast<uint32_t>(ex));
@@ -215,13 +219,30 @@ __device__ __forceinline__ void WalkRuns(int runs, int len, FastDiv by_len, Star
 }
 
 template <typename Off>
-struct Run { Off a, b; int z; };
+struct Run { Off a, b; };
+
+template <typename Off>
+struct Run3 { Off a, b; int c; };
+
+// Asynchronous global -> shared copy of one element (no register round trip).
+template <int Bytes>
+__device__ __forceinline__ void CopyAsync(void* smem, const void* gmem) {
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  if constexpr (Bytes == 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem) : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(dst), "l"(gmem), "n"(Bytes) : "memory");
+  }
+}
+
+__device__ __forceinline__ void WaitAsync() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 template <int Op, typename T, typename CA, typename CB, typename Off>
 __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ TileState<Off> st;
   T* tile = reinterpret_cast<T*>(smem_raw);
+  T* base_tile = tile + args.tile_elems;     // update: destination base values, in run order
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * per_cta;
@@ -235,75 +256,64 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
     const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
     T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
     const bool skip = emit.SkipSource();
-    const bool needs_base = emit.NeedsBase();
-    const int ex = st.ex;
-    if (st.mode == kDirect || skip) {
-      // Runs along X, one per (y, z); a skipped source touches only the destination.
-      const Off sx = st.sx, sy = st.sy, sz = st.sz, dx = st.dx, dy = st.dy, dz = st.dz;
-      const int ey = st.ey;
-      const FastDiv by_y = st.div_y;
-      WalkRuns(ey * st.ez, ex, st.div_x,
+    const bool needs_base = Emit<Op, T, CA, CB>::kReadsBase && emit.NeedsBase();
+    const int ex = st.ex, ey = st.ey;
+    const bool direct = st.mode == kDirect;
+    const int px = st.px, pz = st.pz;
+    const Off dx = st.dx, dy = st.dy, dz = st.dz;
+    const bool dst_linear = st.dst_linear;
+    const FastDiv by_x = st.div_x, by_y = st.div_y;
+    // Destination run r: its tile offset and its destination offset.
+    auto dst_run = [&](int r) {
+      if (dst_linear) return Run<Off>{static_cast<Off>(pz * r), static_cast<Off>(r * dz)};
+      const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
+      const int y = r - z * ey;
+      return Run<Off>{static_cast<Off>(px * y + pz * z), static_cast<Off>(y * dy + z * dz)};
+    };
+    // Load: source runs into tile[x + px * y + pz * z]; base values (update) into base_tile.
+    if (!skip) {
+      const Off sx = st.sx, sy = st.sy, sz = st.sz;
+      const bool linear = st.src_linear;
+      const Off step = direct ? sx : sy;        // source stride along a run
+      const int pitch = direct ? 1 : px;        // tile stride along a run
+      WalkRuns(st.src_runs, st.src_len, st.div_src,
           [&](int r) {
-            const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
-            const int y = r - z * ey;
-            return Run<Off>{static_cast<Off>(y * sy + z * sz), static_cast<Off>(y * dy + z * dz), 0};
+            if (direct) return Run<Off>{static_cast<Off>(r * sz), static_cast<Off>(pz * r)};
+            if (linear) return Run<Off>{static_cast<Off>(r * sx), static_cast<Off>(r)};
+            const int z = static_cast<int>(by_x.Div(static_cast<uint32_t>(r)));
+            const int x = r - z * ex;
+            return Run<Off>{static_cast<Off>(x * sx + z * sz), static_cast<Off>(x + pz * z)};
           },
-          [&](const Run<Off>& run, int x) {
-            const Off at = run.b + x * dx;
+          [&](const Run<Off>& run, int j) { CopyAsync<sizeof(T)>(tile + run.b + j * pitch, src + run.a + j * step); });
+    }
+    if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+      if (needs_base) {
+        const int len = st.dst_len;
+        WalkRuns(st.dst_runs, len, st.div_dst, [&](int r) { return Run<Off>{static_cast<Off>(r * len), dst_run(r).b}; },
+            [&](const Run<Off>& run, int k) { CopyAsync<sizeof(T)>(base_tile + run.a + k, base + run.b + k * dx); });
+      }
+    }
+    WaitAsync();
+    __syncthreads();
+    // Store: destination runs out of the tile.
+    {
+      const int len = st.dst_len;
+      WalkRuns(st.dst_runs, len, st.div_dst,
+          [&](int r) {
+            const Run<Off> run = dst_run(r);
+            return Run3<Off>{run.a, run.b, r * len};
+          },
+          [&](const Run3<Off>& run, int k) {
+            // Linear runs cover (x, y) with x fastest: k = x + ex * y.
+            int at_tile = run.a + k;
+            if (dst_linear) at_tile += (px - ex) * static_cast<int>(by_x.Div(static_cast<uint32_t>(k)));
             T v{}, old{};
-            if (!skip) v = src[run.a + x * sx];
+            if (!skip) v = tile[at_tile];
             if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
-              if (needs_base) old = base[at];
+              if (needs_base) old = base_tile[run.c + k];
             }
-            out[at] = emit(v, old);
+            out[run.b + k * dx] = emit(v, old);
           });
-    } else {
-      // Source runs into tile[x + px * y + pz * z].
-      {
-        const Off sx = st.sx, sy = st.sy, sz = st.sz;
-        const int px = st.px, pz = st.pz;
-        const bool linear = st.src_linear;
-        const FastDiv by_x = st.div_x;
-        WalkRuns(st.src_runs, st.src_len, st.div_src,
-            [&](int r) {
-              if (linear) return Run<Off>{static_cast<Off>(r * sx), static_cast<Off>(r), 0};
-              const int z = static_cast<int>(by_x.Div(static_cast<uint32_t>(r)));
-              const int x = r - z * ex;
-              return Run<Off>{static_cast<Off>(x * sx + z * sz), static_cast<Off>(x + pz * z), 0};
-            },
-            [&](const Run<Off>& run, int j) { tile[run.b + j * px] = src[run.a + j * sy]; });
-      }
-      __syncthreads();
-      // Destination runs out of the tile.
-      {
-        const Off dx = st.dx, dy = st.dy, dz = st.dz;
-        const int px = st.px, pz = st.pz, ey = st.ey;
-        const bool linear = st.dst_linear;
-        const FastDiv by_x = st.div_x, by_y = st.div_y;
-        WalkRuns(st.dst_runs, st.dst_len, st.div_dst,
-            [&](int r) {
-              if (linear) return Run<Off>{static_cast<Off>(pz * r), static_cast<Off>(r * dz), 0};
-              const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
-              const int y = r - z * ey;
-              return Run<Off>{static_cast<Off>(px * y + pz * z), static_cast<Off>(y * dy + z * dz), 0};
-            },
-            [&](const Run<Off>& run, int k) {
-              // Linear runs cover (x, y) with x fastest: k = x + ex * y.
-              int at_tile;
-              if (linear) {
-                const int y = static_cast<int>(by_x.Div(static_cast<uint32_t>(k)));
-                at_tile = run.a + k + (px - ex) * y;
-              } else {
-                at_tile = run.a + k;
-              }
-              const Off at = run.b + k * dx;
-              T old{};
-              if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
-                if (needs_base) old = base[at];
-              }
-              out[at] = emit(tile[at_tile], old);
-            });
-      }
     }
     __syncthreads();
   }
@@ -489,13 +499,14 @@ void Check(cudaError_t status, const char* what) {
   if (status != cudaSuccess) throw std::runtime_error(std::string("CUDA ") + what + ": " + cudaGetErrorString(status));
 }
 
-int MapSharedBytes(const MapRecord* recs, int64_t count, int element_bytes) {
-  int64_t best = 0;
+void MapTileElements(const MapRecord* recs, int64_t count, int64_t* tile, int64_t* box) {
+  *tile = 0;
+  *box = 0;
   for (int64_t i = 0; i < count; ++i) {
-    if (recs[i].mode != kTranspose) continue;
-    best = std::max<int64_t>(best, int64_t{recs[i].t[0] | 1} * recs[i].t[1] * recs[i].t[2] * element_bytes);
+    const int64_t t0 = recs[i].t[0], t1 = recs[i].t[1], t2 = recs[i].t[2];
+    *tile = std::max<int64_t>(*tile, (t0 | 1) * t1 * t2);
+    *box = std::max<int64_t>(*box, t0 * t1 * t2);
   }
-  return static_cast<int>(best);
 }
 
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,

@@ -17,8 +17,10 @@ namespace {
 constexpr uint64_t kExtentLimit = uint64_t{1} << 30;   // per-axis extent kept in int32
 constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap check
 
-// Bytes of shared memory one map tile may stage (before row padding).
+// Bytes of shared memory one map tile may stage (before row padding).  Update
+// tiles also stage the destination's base values, so they get half.
 constexpr int64_t kTileBytes = 32768;
+constexpr int64_t kUpdateTileBytes = 16384;
 
 // Split records so every axis extent fits in int32 and at most kMaxRank axes remain.
 std::vector<Record> SplitForDevice(const Record& record) {
@@ -121,7 +123,7 @@ bool ProveDisjoint(const std::vector<const Record*>& records, uint64_t output_si
 
 int64_t CeilDiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_bytes, int64_t tile_begin) {
+MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int64_t tile_begin) {
   MapRecord out{};
   out.src_off = record.src_off;
   out.dst_off = record.dst_off;
@@ -134,7 +136,6 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int32_t element_byte
   for (std::size_t a = 1; a < rank; ++a) {
     if (AbsStride(record.sstr[a]) < AbsStride(record.sstr[y])) y = a;
   }
-  const int64_t budget = kTileBytes / element_bytes;
   std::vector<std::size_t> rest;
   for (std::size_t a = 0; a < rank; ++a) {
     if (a != x && a != y) rest.push_back(a);
@@ -348,7 +349,8 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
   for (std::size_t i : map_ids) {
     Record fused = records[i];
     Canonicalize(fused, true);
-    MapRecord record = MakeMapRecord(fused, record_slot[i], element_bytes, tiles);
+    MapRecord record = MakeMapRecord(fused, record_slot[i],
+                                     (operation == 1 ? kUpdateTileBytes : kTileBytes) / element_bytes, tiles);
     tiles += MapTiles(record);
     plan.map_wide = plan.map_wide || NeedsWideOffsets(record);
     covered += ElementCount(records[i]);
