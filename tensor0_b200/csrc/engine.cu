@@ -56,6 +56,7 @@ struct TileState {
   int src_linear, dst_linear;
   FastDiv div_x, div_y, div_src, div_dst;   // by ex, by ey, by src_len, by dst_len
   int64_t batch;
+  alignas(16) unsigned char coef[32];       // the tile's coefficients, fetched by the decoding thread
 };
 
 // Thread 0 only: advance the record cursor to the tile and decode it.
@@ -125,6 +126,9 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64
 }
 
 // Per-operation element rule applied when a value reaches the destination.
+// Fetch (decoding thread) stages the tile's coefficients in shared memory;
+// the constructor reads them back.  Kind() selects a specialised store loop:
+// 1 and 2 are the common unit cases, 0 the general rule.
 template <int Op, typename T, typename CA, typename CB>
 struct Emit;
 
@@ -132,10 +136,12 @@ struct Emit;
 template <typename T, typename CA, typename CB>
 struct Emit<kOpCopy, T, CA, CB> {
   static constexpr bool kReadsBase = false;
-  __device__ __forceinline__ Emit(const MapArgs&, int, int64_t) {}
+  __device__ static void Fetch(const MapArgs&, int, int64_t, unsigned char*) {}
+  __device__ __forceinline__ explicit Emit(const unsigned char*) {}
   __device__ __forceinline__ bool SkipSource() const { return false; }
   __device__ __forceinline__ bool NeedsBase() const { return false; }
-  __device__ __forceinline__ T operator()(T v, T) const { return v; }
+  __device__ __forceinline__ int Kind() const { return 1; }
+  template <int K> __device__ __forceinline__ T Apply(T v, T) const { return v; }
 };
 
 // Accumulation into a zeroed output: 0 + c * v, with the zero / one rules.
@@ -144,21 +150,27 @@ struct Emit<kOpAccumulation, T, CA, CB> {
   static constexpr bool kReadsBase = false;
   using Real = typename Elem<T>::Real;
   using C = typename BoundOf<Real, CA>::type;
+  struct Staged { C c; int present; };
   C c;
   bool zero, one;
-  __device__ __forceinline__ Emit(const MapArgs& a, int slot, int64_t batch) {
-    if (slot < 0) {
-      zero = false; one = true; c = C{};
-    } else {
-      c = ReadCoefficient<Real>(static_cast<const CA*>(a.ca), slot, a.ca_count, batch);
-      zero = IsZero(c); one = IsOne(c);
-    }
+  __device__ static void Fetch(const MapArgs& a, int slot, int64_t batch, unsigned char* out) {
+    Staged s{C{}, slot >= 0};
+    if (slot >= 0) s.c = ReadCoefficient<Real>(static_cast<const CA*>(a.ca), slot, a.ca_count, batch);
+    *reinterpret_cast<Staged*>(out) = s;
+  }
+  __device__ __forceinline__ explicit Emit(const unsigned char* staged) {
+    const Staged s = *reinterpret_cast<const Staged*>(staged);
+    c = s.c;
+    zero = s.present && IsZero(c);
+    one = !s.present || IsOne(c);
   }
   __device__ __forceinline__ bool SkipSource() const { return zero; }
   __device__ __forceinline__ bool NeedsBase() const { return false; }
-  __device__ __forceinline__ T operator()(T v, T) const {
-    if (zero) return Zero<T>();
-    return PlusZero(one ? v : Scale(c, v));
+  __device__ __forceinline__ int Kind() const { return zero ? 2 : (one ? 1 : 0); }
+  template <int K> __device__ __forceinline__ T Apply(T v, T) const {
+    if constexpr (K == 2) return Zero<T>();
+    else if constexpr (K == 1) return PlusZero(v);
+    else return PlusZero(Scale(c, v));
   }
 };
 
@@ -171,21 +183,32 @@ struct Emit<kOpUpdate, T, CA, CB> {
   using B = typename BoundOf<Real, CB>::type;
   A a; B b;
   bool a0, a1, b0, b1;
-  __device__ __forceinline__ Emit(const MapArgs& args, int, int64_t batch) {
-    a = ReadCoefficient<Real>(static_cast<const CA*>(args.ca), 0, args.ca_count, batch);
-    b = ReadCoefficient<Real>(static_cast<const CB*>(args.cb), 0, args.cb_count, batch);
+  __device__ static void Fetch(const MapArgs& args, int, int64_t batch, unsigned char* out) {
+    *reinterpret_cast<A*>(out) = ReadCoefficient<Real>(static_cast<const CA*>(args.ca), 0, args.ca_count, batch);
+    *reinterpret_cast<B*>(out + 16) = ReadCoefficient<Real>(static_cast<const CB*>(args.cb), 0, args.cb_count, batch);
+  }
+  __device__ __forceinline__ explicit Emit(const unsigned char* staged) {
+    a = *reinterpret_cast<const A*>(staged);
+    b = *reinterpret_cast<const B*>(staged + 16);
     a0 = IsZero(a); a1 = IsOne(a); b0 = IsZero(b); b1 = IsOne(b);
   }
   __device__ __forceinline__ bool SkipSource() const { return a0; }
   __device__ __forceinline__ bool NeedsBase() const { return !b0; }
-  __device__ __forceinline__ T operator()(T v, T old) const {
-    if (a0) {
-      if (b0) return Zero<T>();
-      return b1 ? old : Scale(b, old);
+  __device__ __forceinline__ int Kind() const { return (a1 && b1) ? 1 : ((a1 && b0) ? 2 : 0); }
+  template <int K> __device__ __forceinline__ T Apply(T v, T old) const {
+    if constexpr (K == 1) {
+      return Add(v, old);
+    } else if constexpr (K == 2) {
+      return v;
+    } else {
+      if (a0) {
+        if (b0) return Zero<T>();
+        return b1 ? old : Scale(b, old);
+      }
+      const T s = a1 ? v : Scale(a, v);
+      if (b0) return s;
+      return Add(s, b1 ? old : Scale(b, old));
     }
-    const T s = a1 ? v : Scale(a, v);
-    if (b0) return s;
-    return Add(s, b1 ? old : Scale(b, old));
   }
 };
 
@@ -238,9 +261,10 @@ __device__ __forceinline__ void CopyAsync(void* smem, const void* gmem) {
 __device__ __forceinline__ void WaitAsync() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 template <int Op, typename T, typename CA, typename CB, typename Off>
-__global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
+__global__ void __launch_bounds__(kThreads, 4) MapKernel(MapArgs args) {
+  using E = Emit<Op, T, CA, CB>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ TileState<Off> st;
+  __shared__ TileState<Off> states[2];        // the current tile and the next one
   T* tile = reinterpret_cast<T*>(smem_raw);
   T* base_tile = tile + args.tile_elems;     // update: destination base values, in run order
   const int64_t total = args.tiles_per_batch * args.batches;
@@ -248,21 +272,28 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
   const int64_t first = static_cast<int64_t>(blockIdx.x) * per_cta;
   const int64_t last = min(total, first + per_cta);
   int64_t cursor = -1;   // record cursor, meaningful in thread 0 only
-  for (int64_t t = first; t < last; ++t) {
-    if (threadIdx.x == 0) DecodeTile<Off>(args, t, cursor, st);
-    __syncthreads();
-    const Emit<Op, T, CA, CB> emit(args, st.slot, st.batch);
+  if (threadIdx.x == 0 && first < last) {
+    DecodeTile<Off>(args, first, cursor, states[0]);
+    E::Fetch(args, states[0].slot, states[0].batch, states[0].coef);
+  }
+  __syncthreads();
+  int buffer = 0;
+  for (int64_t t = first; t < last; ++t, buffer ^= 1) {
+    const TileState<Off>& st = states[buffer];
+    const E emit(st.coef);
     const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
     const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
     T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
     const bool skip = emit.SkipSource();
-    const bool needs_base = Emit<Op, T, CA, CB>::kReadsBase && emit.NeedsBase();
+    const bool needs_base = E::kReadsBase && emit.NeedsBase();
     const int ex = st.ex, ey = st.ey;
     const bool direct = st.mode == kDirect;
     const int px = st.px, pz = st.pz;
     const Off dx = st.dx, dy = st.dy, dz = st.dz;
     const bool dst_linear = st.dst_linear;
     const FastDiv by_x = st.div_x, by_y = st.div_y;
+    const int dst_runs = st.dst_runs, dst_len = st.dst_len;
+    const FastDiv div_dst = st.div_dst;
     // Destination run r: its tile offset and its destination offset.
     auto dst_run = [&](int r) {
       if (dst_linear) return Run<Off>{static_cast<Off>(pz * r), static_cast<Off>(r * dz)};
@@ -286,22 +317,28 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
           },
           [&](const Run<Off>& run, int j) { CopyAsync<sizeof(T)>(tile + run.b + j * pitch, src + run.a + j * step); });
     }
-    if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+    if constexpr (E::kReadsBase) {
       if (needs_base) {
-        const int len = st.dst_len;
-        WalkRuns(st.dst_runs, len, st.div_dst, [&](int r) { return Run<Off>{static_cast<Off>(r * len), dst_run(r).b}; },
+        WalkRuns(dst_runs, dst_len, div_dst,
+            [&](int r) { return Run<Off>{static_cast<Off>(r * dst_len), dst_run(r).b}; },
             [&](const Run<Off>& run, int k) { CopyAsync<sizeof(T)>(base_tile + run.a + k, base + run.b + k * dx); });
       }
     }
+    // While the copies fly, the decoding thread prepares the next tile.
+    if (threadIdx.x == 0 && t + 1 < last) {
+      TileState<Off>& next = states[buffer ^ 1];
+      DecodeTile<Off>(args, t + 1, cursor, next);
+      E::Fetch(args, next.slot, next.batch, next.coef);
+    }
     WaitAsync();
     __syncthreads();
-    // Store: destination runs out of the tile.
-    {
-      const int len = st.dst_len;
-      WalkRuns(st.dst_runs, len, st.div_dst,
+    // Store: destination runs out of the tile, with the rule specialised per kind.
+    auto store = [&](auto kind) {
+      constexpr int K = decltype(kind)::value;
+      WalkRuns(dst_runs, dst_len, div_dst,
           [&](int r) {
             const Run<Off> run = dst_run(r);
-            return Run3<Off>{run.a, run.b, r * len};
+            return Run3<Off>{run.a, run.b, r * dst_len};
           },
           [&](const Run3<Off>& run, int k) {
             // Linear runs cover (x, y) with x fastest: k = x + ex * y.
@@ -309,11 +346,16 @@ __global__ void __launch_bounds__(kThreads, 6) MapKernel(MapArgs args) {
             if (dst_linear) at_tile += (px - ex) * static_cast<int>(by_x.Div(static_cast<uint32_t>(k)));
             T v{}, old{};
             if (!skip) v = tile[at_tile];
-            if constexpr (Emit<Op, T, CA, CB>::kReadsBase) {
+            if constexpr (E::kReadsBase) {
               if (needs_base) old = base_tile[run.c + k];
             }
-            out[run.b + k * dx] = emit(v, old);
+            out[run.b + k * dx] = emit.template Apply<K>(v, old);
           });
+    };
+    switch (emit.Kind()) {
+      case 1: store(std::integral_constant<int, 1>{}); break;
+      case 2: store(std::integral_constant<int, 2>{}); break;
+      default: store(std::integral_constant<int, 0>{}); break;
     }
     __syncthreads();
   }
