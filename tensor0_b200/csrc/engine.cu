@@ -4,13 +4,14 @@
 // The map kernel is one persistent grid over every tile of every record of
 // every batch; each CTA walks a contiguous range of tiles.  A tile is a box
 // over the record's destination-innermost axis X, its source-innermost axis Y
-// and one further axis Z.  One thread decodes the tile (record cursor, chunk
-// coordinates, outer axes) into shared memory.  The CTA then copies the tile
-// in contiguous runs: source runs (Y, continued by Z when Z follows Y in the
-// source) into shared memory, and destination runs (X, continued by Y when Y
-// follows X in the destination) out of it.  Lanes stride each run, so reads
-// and writes are coalesced and each element costs a few integer operations.
-// When X and Y coincide the tile is copied run by run without staging.
+// and one further axis Z.  One thread decodes the tile with host-computed
+// division constants into two run lists: the source runs (along Y, continued
+// by Z when Z follows Y in the source), copied asynchronously into a
+// destination-ordered shared-memory tile, and the destination runs (rows
+// along X, or whole (x, y) planes when they are contiguous on both sides),
+// written out of it.  Warps take runs with constant address increments and
+// lanes stride each run, so reads and writes are coalesced and an element
+// costs its memory instruction and an addition or two.
 #include "engine.h"
 
 #include "arith.cuh"
@@ -27,102 +28,96 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// Division by a runtime divisor in [1, 2^24) for dividends below 2^24:
-// n / d = (umulhi(n, m) + n) >> l with l = ceil(log2 d) and
-// m = floor(2^32 (2^l - d) / d) + 1 (round-up multiplier method).
+// Division by a constant computed on the host (MakeDivision).
 struct FastDiv {
   uint32_t m, l;
-  __device__ __forceinline__ FastDiv() = default;
-  __device__ __forceinline__ FastDiv(uint32_t magic, uint32_t shift) : m(magic), l(shift) {}
-  __device__ __forceinline__ static FastDiv Of(uint32_t divisor) {
-    const uint32_t shift = 32 - __clz(divisor - 1);
-    const uint64_t one = 1;
-    return FastDiv(static_cast<uint32_t>(((one << 32) * ((one << shift) - divisor)) / divisor + 1), shift);
-  }
   __device__ __forceinline__ uint32_t Div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
 };
 
+__device__ __forceinline__ FastDiv Division(const DivisionConstants& c) { return FastDiv{c.magic, c.shift}; }
+
+// The runs one phase of a tile copies: run (a, b), a in [0, na), b in
+// [0, nb), starts at global offset a * ga + b * gb and shared-memory index
+// a * sa + b * sb; its element j in [0, len) sits at + j * gj and + j * sj.
+template <typename Off>
+struct Runs {
+  Off ga, gb, gj;
+  int sa, sb, sj;
+  int na, nb, len;
+  FastDiv by_na, by_len;   // used when the runs are packed (few or short runs)
+};
+
 // A decoded tile, shared by the CTA.  In-tile offsets use Off (int32 unless
-// the plan marked a record wide).
+// the plan marked a record wide).  Shared memory holds the tile in
+// destination order: element (x, y, z) at x + px * y + pz * z, px = ex | 1
+// (odd, so source runs, which step px, hit distinct banks) and pz = px * ey.
 template <typename Off>
 struct TileState {
   int64_t so, dof;        // element offsets of the tile origin, batch included
-  Off sx, sy, sz, dx, dy, dz;
-  int ex, ey, ez;         // tile extents (edge tiles are smaller)
-  int px, pz;             // shared-memory pitches along Y (odd, >= ex) and Z
-  int mode, slot;
-  int src_runs, src_len;  // source runs: ex runs of ey*ez (Z follows Y) or ex*ez runs of ey
-  int dst_runs, dst_len;  // destination runs: ez runs of ex*ey (Y follows X) or ey*ez runs of ex
-  int src_linear, dst_linear;
-  FastDiv div_x, div_y, div_src, div_dst;   // by ex, by ey, by src_len, by dst_len
+  Runs<Off> load;         // source runs into shared memory
+  Runs<Off> store;        // destination runs out of shared memory (also the update's base loads)
   int64_t batch;
-  alignas(16) unsigned char coef[32];       // the tile's coefficients, fetched by the decoding thread
+  int slot;
+  alignas(16) unsigned char coef[32];   // the tile's coefficients, fetched by the decoding thread
 };
 
-// Thread 0 only: advance the record cursor to the tile and decode it.
+// Thread 0 only: decode tile `local` of record `rec` in `batch`.
 template <typename Off>
-__device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t tile, int64_t& cursor, TileState<Off>& s) {
-  const int64_t batch = tile / a.tiles_per_batch;
-  const int64_t local = tile - batch * a.tiles_per_batch;
-  if (cursor < 0 || a.recs[cursor].tile_begin > local) {
-    int64_t lo = 0, hi = a.nrec - 1;
-    while (lo < hi) {
-      const int64_t mid = (lo + hi + 1) >> 1;
-      if (a.recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
-    }
-    cursor = lo;
-  }
-  while (cursor + 1 < a.nrec && a.recs[cursor + 1].tile_begin <= local) ++cursor;
-  const MapRecord& r = a.recs[cursor];
+__device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_t batch, int64_t local,
+                                           TileState<Off>& s) {
+  const MapRecord& r = a.recs[rec];
   uint32_t q = static_cast<uint32_t>(local - r.tile_begin);
-  const uint32_t c0 = r.c[0], c1 = r.c[1], c2 = r.c[2];
-  const uint32_t cx = q % c0; q /= c0;
-  const uint32_t cy = q % c1; q /= c1;
-  const uint32_t cz = q % c2; q /= c2;
+  uint32_t chunk[3];
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const uint32_t next = Division(r.div_tiles[i]).Div(q);
+    chunk[i] = q - next * static_cast<uint32_t>(r.c[i]);
+    q = next;
+  }
   int64_t so = r.src_off + batch * a.src_size;
   int64_t dof = r.dst_off + batch * a.out_size;
   for (int i = 0; i < r.nouter; ++i) {
-    const uint32_t n = static_cast<uint32_t>(r.n[3 + i]);
-    const uint32_t idx = q % n;
-    q /= n;
-    so += static_cast<int64_t>(idx) * r.s[3 + i];
-    dof += static_cast<int64_t>(idx) * r.d[3 + i];
+    const uint32_t next = Division(r.div_tiles[3 + i]).Div(q);
+    const int64_t idx = q - next * static_cast<uint32_t>(r.n[3 + i]);
+    q = next;
+    so += idx * r.s[3 + i];
+    dof += idx * r.d[3 + i];
   }
-  const int x0 = cx * r.t[0], y0 = cy * r.t[1], z0 = cz * r.t[2];
-  const int ex = min(r.t[0], r.n[0] - x0);
-  const int ey = min(r.t[1], r.n[1] - y0);
+  const bool last_x = static_cast<int>(chunk[0]) == r.c[0] - 1;
+  const bool last_y = static_cast<int>(chunk[1]) == r.c[1] - 1;
+  const int ex = last_x ? r.edge[0] : r.t[0];
+  const int ey = last_y ? r.edge[1] : r.t[1];
+  const int z0 = static_cast<int>(chunk[2]) * r.t[2];
   const int ez = min(r.t[2], r.n[2] - z0);
-  s.ex = ex; s.ey = ey; s.ez = ez;
+  const int64_t x0 = static_cast<int64_t>(chunk[0]) * r.t[0], y0 = static_cast<int64_t>(chunk[1]) * r.t[1];
   s.so = so + x0 * r.s[0] + y0 * r.s[1] + z0 * r.s[2];
   s.dof = dof + x0 * r.d[0] + y0 * r.d[1] + z0 * r.d[2];
-  s.sx = static_cast<Off>(r.s[0]); s.sy = static_cast<Off>(r.s[1]); s.sz = static_cast<Off>(r.s[2]);
-  s.dx = static_cast<Off>(r.d[0]); s.dy = static_cast<Off>(r.d[1]); s.dz = static_cast<Off>(r.d[2]);
-  s.px = r.t[0] | 1;
-  s.pz = s.px * r.t[1];
-  s.mode = r.mode;
-  s.slot = r.coef_slot;
-  // Z continues the source run of Y when sz = ey * sy and the shared-memory
-  // Z pitch equals px * ey (a full-height tile); Y continues the destination
-  // run of X when dy = ex * dx.
-  s.src_linear = ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ey == r.t[1];
-  s.dst_linear = ey > 1 && r.d[1] == static_cast<int64_t>(ex) * r.d[0];
-  if (r.mode == kDirect) {
-    // Runs along X on both sides, one per (y, z).
-    s.src_linear = 0;
-    s.dst_linear = 0;
-    s.src_runs = ey * ez;
-    s.src_len = ex;
+  const Off sx = static_cast<Off>(r.s[0]), sy = static_cast<Off>(r.s[1]), sz = static_cast<Off>(r.s[2]);
+  const Off dx = static_cast<Off>(r.d[0]), dy = static_cast<Off>(r.d[1]), dz = static_cast<Off>(r.d[2]);
+  const int px = ex | 1, pz = px * ey;
+  const FastDiv by_x = Division(r.div_extent[last_x ? 1 : 0]);
+  const FastDiv by_y = Division(r.div_extent[last_y ? 3 : 2]);
+  // Destination: when (x, y) is contiguous on both sides (an odd ex needs no
+  // padding) each z plane is one run, else (y, z) rows of ex.
+  Runs<Off>& w = s.store;
+  if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kThreads) {
+    w = Runs<Off>{dz, 0, dx, pz, 0, 1, ez, 1, ex * ey, FastDiv{0, 0}, FastDiv{0, 0}};
   } else {
-    s.src_runs = s.src_linear ? ex : ex * ez;
-    s.src_len = s.src_linear ? ey * ez : ey;
+    w = Runs<Off>{dy, dz, dx, px, pz, 1, ey, ez, ex, by_y, by_x};
   }
-  s.dst_runs = s.dst_linear ? ez : ey * ez;
-  s.dst_len = s.dst_linear ? ex * ey : ex;
-  s.div_x = FastDiv::Of(static_cast<uint32_t>(ex));
-  s.div_y = FastDiv::Of(static_cast<uint32_t>(ey));
-  s.div_src = FastDiv::Of(static_cast<uint32_t>(s.src_len));
-  s.div_dst = FastDiv::Of(static_cast<uint32_t>(s.dst_len));
+  // Source.
+  Runs<Off>& l = s.load;
+  if (r.mode == kDirect) {
+    // X is innermost on both sides: the source runs are the destination rows.
+    l = Runs<Off>{sy, sz, sx, px, pz, 1, ey, ez, ex, by_y, by_x};
+  } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kWarps && ey * ez >= 32) {
+    // Z continues Y in the source (and, as pz = px * ey, in shared memory).
+    l = Runs<Off>{sx, 0, sy, 1, 0, px, ex, 1, ey * ez, FastDiv{0, 0}, FastDiv{0, 0}};
+  } else {
+    l = Runs<Off>{sx, sz, sy, 1, pz, px, ex, ez, ey, by_x, by_y};
+  }
   s.batch = batch;
+  s.slot = r.coef_slot;
 }
 
 // Per-operation element rule applied when a value reaches the destination.
@@ -212,150 +207,176 @@ struct Emit<kOpUpdate, T, CA, CB> {
   }
 };
 
-// Walk `runs` runs of `len` elements.  Runs of 32 elements or more take a
-// whole warp and lanes stride them (unrolled, so several loads are in flight);
-// shorter runs are packed several to a warp, one element per lane.
-// start(run) -> per-run state; f(state, j) handles element j of the run.
-template <typename StartF, typename F>
-__device__ __forceinline__ void WalkRuns(int runs, int len, FastDiv by_len, StartF&& start, F&& f) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (len >= 32) {
-    for (int r = warp; r < runs; r += kWarps) {
-      const auto state = start(r);
-#pragma unroll 4
-      for (int j = lane; j < len; j += 32) f(state, j);
+// This thread's elements j = first_j, first_j + kStep, ... of one run.  kG
+// is the global step when known at compile time (1: unit stride, the usual
+// case, so the unrolled copies address with immediate offsets), or 0 for gj.
+template <typename Off, int kG, int kStep, typename ElemF>
+__device__ __forceinline__ void RunElements(Off g, int s, int j, int len, Off gj, int sj, ElemF& elem) {
+  const Off gs = kStep * (kG != 0 ? static_cast<Off>(kG) : gj);
+  const int ss = kStep * sj;
+  for (; j + 3 * kStep < len; j += 4 * kStep, g += 4 * gs, s += 4 * ss) {
+    elem(g, s);
+    elem(g + gs, s + ss);
+    elem(g + 2 * gs, s + 2 * ss);
+    elem(g + 3 * gs, s + 3 * ss);
+  }
+  for (; j < len; j += kStep, g += gs, s += ss) elem(g, s);
+}
+
+// Walk every element of a phase's runs; elem(g, s) moves one element.  The
+// CTA's threads are spread so every warp has work:
+//   * na >= warps, len >= 32: a warp per run; warps stride a, then b, with
+//                             constant increments (no division per run);
+//   * len >= threads:         the whole CTA strides each run in turn;
+//   * len >= 32:              a warp per run over the flattened (a, b);
+//   * otherwise:              the runs are packed end to end and the threads
+//                             stride the sequence.
+template <typename Off, int kG, typename ElemF>
+__device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
+  const int na = w.na, nb = w.nb, len = w.len;
+  if (len >= 32 && na >= kWarps) {
+    const Off gstep = kWarps * w.ga;
+    const int sstep = kWarps * w.sa;
+    for (int b = 0; b < nb; ++b) {
+      Off g = warp * w.ga + b * w.gb + lane * g1;
+      int s = warp * w.sa + b * w.sb + lane * w.sj;
+      for (int a = warp; a < na; a += kWarps, g += gstep, s += sstep) {
+        RunElements<Off, kG, 32>(g, s, lane, len, w.gj, w.sj, elem);
+      }
+    }
+  } else if (len >= kThreads) {
+    for (int b = 0; b < nb; ++b) {
+      for (int a = 0; a < na; ++a) {
+        RunElements<Off, kG, kThreads>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
+                                       w.gj, w.sj, elem);
+      }
+    }
+  } else if (len >= 32) {
+    for (int r = warp; r < na * nb; r += kWarps) {
+      const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
+      const int a = r - b * na;
+      RunElements<Off, kG, 32>(a * w.ga + b * w.gb + lane * g1, a * w.sa + b * w.sb + lane * w.sj, lane, len,
+                               w.gj, w.sj, elem);
     }
   } else {
-    // Element e of the packed sequence: run e / len, element e % len.
-    const int total = runs * len;
-    for (int e0 = warp * 32; e0 < total; e0 += kThreads * 4) {
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int e = e0 + u * kThreads + lane;
-        if (e < total) {
-          const int r = static_cast<int>(by_len.Div(static_cast<uint32_t>(e)));
-          f(start(r), e - r * len);
-        }
-      }
+    const int total = na * nb * len;
+    for (int f = tid; f < total; f += kThreads) {
+      const int r = static_cast<int>(w.by_len.Div(static_cast<uint32_t>(f)));
+      const int j = f - r * len;
+      const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
+      const int a = r - b * na;
+      elem(a * w.ga + b * w.gb + j * w.gj, a * w.sa + b * w.sb + j * w.sj);
     }
   }
 }
 
-template <typename Off>
-struct Run { Off a, b; };
-
-template <typename Off>
-struct Run3 { Off a, b; int c; };
+template <typename Off, typename ElemF>
+__device__ __forceinline__ void Walk(const Runs<Off>& w, ElemF&& elem) {
+  if (w.gj == 1) WalkRuns<Off, 1>(w, elem);
+  else WalkRuns<Off, 0>(w, elem);
+}
 
 // Asynchronous global -> shared copy of one element (no register round trip).
+// The copies are ordered against shared-memory reads by WaitAsync and the
+// CTA barrier that follows it.
 template <int Bytes>
-__device__ __forceinline__ void CopyAsync(void* smem, const void* gmem) {
-  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+__device__ __forceinline__ void CopyAsync(uint32_t smem, const void* gmem) {
   if constexpr (Bytes == 16) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem) : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem), "l"(gmem));
   } else {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(dst), "l"(gmem), "n"(Bytes) : "memory");
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem), "l"(gmem), "n"(Bytes));
   }
 }
 
 __device__ __forceinline__ void WaitAsync() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
+// Issue the asynchronous loads of one tile: the source runs into the tile
+// and, for update, the destination's base values into the same positions of
+// the base buffer.
+template <typename E, typename T, typename Off>
+__device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Off>& st, uint32_t tile_s,
+                                         uint32_t base_s) {
+  const E emit(st.coef);
+  if (!emit.SkipSource()) {
+    const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
+    Walk<Off>(st.load, [&](Off g, int s) { CopyAsync<sizeof(T)>(tile_s + s * static_cast<int>(sizeof(T)), src + g); });
+  }
+  if constexpr (E::kReadsBase) {
+    if (emit.NeedsBase()) {
+      const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
+      Walk<Off>(st.store, [&](Off g, int s) { CopyAsync<sizeof(T)>(base_s + s * static_cast<int>(sizeof(T)), base + g); });
+    }
+  }
+}
+
+// One persistent CTA walks a contiguous range of tiles.  Per tile: issue the
+// asynchronous loads, let thread 0 decode the next tile while they fly, wait,
+// then write the destination runs out of shared memory.
 template <int Op, typename T, typename CA, typename CB, typename Off>
 __global__ void __launch_bounds__(kThreads, 4) MapKernel(MapArgs args) {
   using E = Emit<Op, T, CA, CB>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ TileState<Off> states[2];        // the current tile and the next one
+  __shared__ int64_t cursor[3];               // decoding thread: record, batch, tile within the batch
   T* tile = reinterpret_cast<T*>(smem_raw);
-  T* base_tile = tile + args.tile_elems;     // update: destination base values, in run order
+  T* base_tile = tile + args.tile_elems;      // update: destination base values, same layout
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * per_cta;
-  const int64_t last = min(total, first + per_cta);
-  int64_t cursor = -1;   // record cursor, meaningful in thread 0 only
-  if (threadIdx.x == 0 && first < last) {
-    DecodeTile<Off>(args, first, cursor, states[0]);
+  const int64_t count = first < total ? min(total, first + per_cta) - first : 0;
+  if (threadIdx.x == 0 && count > 0) {
+    const int64_t batch = first / args.tiles_per_batch;
+    const int64_t local = first - batch * args.tiles_per_batch;
+    int64_t lo = 0, hi = args.nrec - 1;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (args.recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
+    }
+    cursor[0] = lo; cursor[1] = batch; cursor[2] = local;
+    DecodeTile<Off>(args, lo, batch, local, states[0]);
     E::Fetch(args, states[0].slot, states[0].batch, states[0].coef);
   }
   __syncthreads();
-  int buffer = 0;
-  for (int64_t t = first; t < last; ++t, buffer ^= 1) {
-    const TileState<Off>& st = states[buffer];
-    const E emit(st.coef);
-    const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
-    const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
-    T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
-    const bool skip = emit.SkipSource();
-    const bool needs_base = E::kReadsBase && emit.NeedsBase();
-    const int ex = st.ex, ey = st.ey;
-    const bool direct = st.mode == kDirect;
-    const int px = st.px, pz = st.pz;
-    const Off dx = st.dx, dy = st.dy, dz = st.dz;
-    const bool dst_linear = st.dst_linear;
-    const FastDiv by_x = st.div_x, by_y = st.div_y;
-    const int dst_runs = st.dst_runs, dst_len = st.dst_len;
-    const FastDiv div_dst = st.div_dst;
-    // Destination run r: its tile offset and its destination offset.
-    auto dst_run = [&](int r) {
-      if (dst_linear) return Run<Off>{static_cast<Off>(pz * r), static_cast<Off>(r * dz)};
-      const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
-      const int y = r - z * ey;
-      return Run<Off>{static_cast<Off>(px * y + pz * z), static_cast<Off>(y * dy + z * dz)};
-    };
-    // Load: source runs into tile[x + px * y + pz * z]; base values (update) into base_tile.
-    if (!skip) {
-      const Off sx = st.sx, sy = st.sy, sz = st.sz;
-      const bool linear = st.src_linear;
-      const Off step = direct ? sx : sy;        // source stride along a run
-      const int pitch = direct ? 1 : px;        // tile stride along a run
-      WalkRuns(st.src_runs, st.src_len, st.div_src,
-          [&](int r) {
-            if (direct) return Run<Off>{static_cast<Off>(r * sz), static_cast<Off>(pz * r)};
-            if (linear) return Run<Off>{static_cast<Off>(r * sx), static_cast<Off>(r)};
-            const int z = static_cast<int>(by_x.Div(static_cast<uint32_t>(r)));
-            const int x = r - z * ex;
-            return Run<Off>{static_cast<Off>(x * sx + z * sz), static_cast<Off>(x + pz * z)};
-          },
-          [&](const Run<Off>& run, int j) { CopyAsync<sizeof(T)>(tile + run.b + j * pitch, src + run.a + j * step); });
-    }
-    if constexpr (E::kReadsBase) {
-      if (needs_base) {
-        WalkRuns(dst_runs, dst_len, div_dst,
-            [&](int r) { return Run<Off>{static_cast<Off>(r * dst_len), dst_run(r).b}; },
-            [&](const Run<Off>& run, int k) { CopyAsync<sizeof(T)>(base_tile + run.a + k, base + run.b + k * dx); });
-      }
-    }
+  for (int64_t i = 0; i < count; ++i) {
+    const TileState<Off>& st = states[i & 1];
+    LoadTile<E, T, Off>(args, st, static_cast<uint32_t>(__cvta_generic_to_shared(tile)),
+                        static_cast<uint32_t>(__cvta_generic_to_shared(base_tile)));
     // While the copies fly, the decoding thread prepares the next tile.
-    if (threadIdx.x == 0 && t + 1 < last) {
-      TileState<Off>& next = states[buffer ^ 1];
-      DecodeTile<Off>(args, t + 1, cursor, next);
+    if (threadIdx.x == 0 && i + 1 < count) {
+      int64_t rec = cursor[0], batch = cursor[1], local = cursor[2] + 1;
+      if (local == args.tiles_per_batch) { local = 0; ++batch; rec = 0; }
+      while (rec + 1 < args.nrec && args.recs[rec + 1].tile_begin <= local) ++rec;
+      cursor[0] = rec; cursor[1] = batch; cursor[2] = local;
+      TileState<Off>& next = states[(i + 1) & 1];
+      DecodeTile<Off>(args, rec, batch, local, next);
       E::Fetch(args, next.slot, next.batch, next.coef);
     }
     WaitAsync();
     __syncthreads();
     // Store: destination runs out of the tile, with the rule specialised per kind.
-    auto store = [&](auto kind) {
-      constexpr int K = decltype(kind)::value;
-      WalkRuns(dst_runs, dst_len, div_dst,
-          [&](int r) {
-            const Run<Off> run = dst_run(r);
-            return Run3<Off>{run.a, run.b, r * dst_len};
-          },
-          [&](const Run3<Off>& run, int k) {
-            // Linear runs cover (x, y) with x fastest: k = x + ex * y.
-            int at_tile = run.a + k;
-            if (dst_linear) at_tile += (px - ex) * static_cast<int>(by_x.Div(static_cast<uint32_t>(k)));
-            T v{}, old{};
-            if (!skip) v = tile[at_tile];
-            if constexpr (E::kReadsBase) {
-              if (needs_base) old = base_tile[run.c + k];
-            }
-            out[run.b + k * dx] = emit.template Apply<K>(v, old);
-          });
-    };
-    switch (emit.Kind()) {
-      case 1: store(std::integral_constant<int, 1>{}); break;
-      case 2: store(std::integral_constant<int, 2>{}); break;
-      default: store(std::integral_constant<int, 0>{}); break;
+    {
+      const E emit(st.coef);
+      const bool skip = emit.SkipSource();
+      const bool needs_base = E::kReadsBase && emit.NeedsBase();
+      T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
+      auto store = [&](auto kind) {
+        constexpr int K = decltype(kind)::value;
+        Walk<Off>(st.store, [&](Off g, int s) {
+          T v{}, old{};
+          if (!skip) v = tile[s];
+          if constexpr (E::kReadsBase) {
+            if (needs_base) old = base_tile[s];
+          }
+          out[g] = emit.template Apply<K>(v, old);
+        });
+      };
+      switch (emit.Kind()) {
+        case 1: store(std::integral_constant<int, 1>{}); break;
+        case 2: store(std::integral_constant<int, 2>{}); break;
+        default: store(std::integral_constant<int, 0>{}); break;
+      }
     }
     __syncthreads();
   }

@@ -123,6 +123,19 @@ bool ProveDisjoint(const std::vector<const Record*>& records, uint64_t output_si
 
 int64_t CeilDiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Division constants the device uses to decode a tile without dividing.
+void SetDivisions(MapRecord& r) {
+  for (int i = 0; i < kMaxRank; ++i) {
+    const int32_t divisor = i < 3 ? r.c[i] : (i - 3 < r.nouter ? r.n[i] : 1);
+    r.div_tiles[i] = MakeDivision(static_cast<uint32_t>(std::max(divisor, 1)));
+  }
+  for (int i = 0; i < 2; ++i) {
+    r.edge[i] = r.n[i] - (r.c[i] - 1) * r.t[i];
+    r.div_extent[2 * i] = MakeDivision(static_cast<uint32_t>(std::max(r.t[i], 1)));
+    r.div_extent[2 * i + 1] = MakeDivision(static_cast<uint32_t>(std::max(r.edge[i], 1)));
+  }
+}
+
 MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int64_t tile_begin) {
   MapRecord out{};
   out.src_off = record.src_off;
@@ -151,6 +164,7 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int6
     out.t[0] = out.t[1] = out.t[2] = 1;
     out.c[0] = out.c[1] = out.c[2] = 1;
     out.nouter = 0;
+    SetDivisions(out);
     return out;
   }
   put(0, x);
@@ -198,6 +212,7 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int6
   for (int i = 0; i < 3; ++i) out.c[i] = static_cast<int32_t>(CeilDiv(out.n[i], out.t[i]));
   out.nouter = static_cast<int32_t>(rest.size());
   for (std::size_t i = 0; i < rest.size(); ++i) put(3 + static_cast<int>(i), rest[i]);
+  SetDivisions(out);
   return out;
 }
 

@@ -26,6 +26,21 @@ namespace t0b {
 
 constexpr int kMaxRank = 8;
 
+// Constants for dividing 32-bit values below 2^31 by a fixed divisor d >= 1:
+// n / d = (umulhi(n, magic) + n) >> shift with shift = ceil(log2 d) and
+// magic = floor(2^32 (2^shift - d) / d) + 1 (the round-up multiplier method).
+struct DivisionConstants {
+  uint32_t magic;
+  uint32_t shift;
+};
+
+inline DivisionConstants MakeDivision(uint32_t divisor) {
+  uint32_t shift = 0;
+  while ((uint64_t{1} << shift) < divisor) ++shift;
+  const uint64_t magic = ((uint64_t{1} << 32) * ((uint64_t{1} << shift) - divisor)) / divisor + 1;
+  return DivisionConstants{static_cast<uint32_t>(magic), shift};
+}
+
 // Map-engine record (device layout; shared by host and device code).
 struct alignas(16) MapRecord {
   int64_t src_off;
@@ -40,6 +55,12 @@ struct alignas(16) MapRecord {
   int32_t mode;         // kTranspose or kDirect
   int32_t coef_slot;    // coefficient row, or -1 for factor one
   int32_t pad_;
+  // Splitting a tile index: division by c[0], c[1], c[2], then by n[3], n[4], ...
+  DivisionConstants div_tiles[kMaxRank];
+  // Extents of the last tile along X and Y, and division by t[0], edge[0], t[1], edge[1].
+  int32_t edge[2];
+  DivisionConstants div_extent[4];
+  int32_t pad2_[2];
 };
 
 enum MapMode : int32_t { kTranspose = 0, kDirect = 1 };
@@ -86,7 +107,7 @@ struct TableHeader {
   int64_t reserved[5];
 };
 
-constexpr int64_t kTableVersion = 0x7430620001;
+constexpr int64_t kTableVersion = 0x7430620002;
 
 struct Wave {               // consecutive groups that may run concurrently
   int64_t group_begin, group_end;
