@@ -207,20 +207,26 @@ struct Emit<kOpUpdate, T, CA, CB> {
   }
 };
 
-// This thread's elements j = first_j, first_j + kStep, ... of one run.  kG
-// is the global step when known at compile time (1: unit stride, the usual
-// case, so the unrolled copies address with immediate offsets), or 0 for gj.
+// This thread's elements j = first_j, first_j + kStep, ... of one run
+// (first_j < kStep).  The number of unrolled blocks is the same for every
+// thread of the warp, and the last up-to-four elements are predicated, so
+// lanes never split between the two paths.  kG is the global step when known
+// at compile time (1: unit stride, the usual case, so the unrolled copies
+// address with immediate offsets), or 0 for gj.
 template <typename Off, int kG, int kStep, typename ElemF>
 __device__ __forceinline__ void RunElements(Off g, int s, int j, int len, Off gj, int sj, ElemF& elem) {
   const Off gs = kStep * (kG != 0 ? static_cast<Off>(kG) : gj);
   const int ss = kStep * sj;
-  for (; j + 3 * kStep < len; j += 4 * kStep, g += 4 * gs, s += 4 * ss) {
+  for (int block = len / (4 * kStep); block > 0; --block, j += 4 * kStep, g += 4 * gs, s += 4 * ss) {
     elem(g, s);
     elem(g + gs, s + ss);
     elem(g + 2 * gs, s + 2 * ss);
     elem(g + 3 * gs, s + 3 * ss);
   }
-  for (; j < len; j += kStep, g += gs, s += ss) elem(g, s);
+  if (j < len) elem(g, s);
+  if (j + kStep < len) elem(g + gs, s + ss);
+  if (j + 2 * kStep < len) elem(g + 2 * gs, s + 2 * ss);
+  if (j + 3 * kStep < len) elem(g + 3 * gs, s + 3 * ss);
 }
 
 // Walk every element of a phase's runs; elem(g, s) moves one element.  The
@@ -272,8 +278,11 @@ __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
   }
 }
 
+// `runs` lives in shared memory; the walk uses a register copy, which stores
+// through generic pointers cannot alias.
 template <typename Off, typename ElemF>
-__device__ __forceinline__ void Walk(const Runs<Off>& w, ElemF&& elem) {
+__device__ __forceinline__ void Walk(const Runs<Off>& runs, ElemF&& elem) {
+  const Runs<Off> w = runs;
   if (w.gj == 1) WalkRuns<Off, 1>(w, elem);
   else WalkRuns<Off, 0>(w, elem);
 }
