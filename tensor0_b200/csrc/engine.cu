@@ -27,6 +27,9 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+#ifndef T0B_MAP_MIN_BLOCKS
+#define T0B_MAP_MIN_BLOCKS 4   // map CTAs per SM the register budget is sized for
+#endif
 
 // Division by a constant computed on the host (MakeDivision).
 struct FastDiv {
@@ -36,6 +39,9 @@ struct FastDiv {
 
 __device__ __forceinline__ FastDiv Division(const DivisionConstants& c) { return FastDiv{c.magic, c.shift}; }
 
+// "Division" by 2^31: every run index of a single-plane run list is in plane 0.
+constexpr FastDiv kSinglePlane{0, 31};
+
 // The runs one phase of a tile copies: run (a, b), a in [0, na), b in
 // [0, nb), starts at global offset a * ga + b * gb and shared-memory index
 // a * sa + b * sb; its element j in [0, len) sits at + j * gj and + j * sj.
@@ -44,7 +50,8 @@ struct Runs {
   Off ga, gb, gj;
   int sa, sb, sj;
   int na, nb, len;
-  FastDiv by_na, by_len;   // used when the runs are packed (few or short runs)
+  FastDiv by_na;           // run index -> b
+  FastDiv by_len;          // element index -> run (packed short runs only)
 };
 
 // A decoded tile, shared by the CTA.  In-tile offsets use Off (int32 unless
@@ -101,7 +108,7 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   // padding) each z plane is one run, else (y, z) rows of ex.
   Runs<Off>& w = s.store;
   if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kThreads) {
-    w = Runs<Off>{dz, 0, dx, pz, 0, 1, ez, 1, ex * ey, FastDiv{0, 0}, FastDiv{0, 0}};
+    w = Runs<Off>{dz, 0, dx, pz, 0, 1, ez, 1, ex * ey, kSinglePlane, FastDiv{0, 0}};
   } else {
     w = Runs<Off>{dy, dz, dx, px, pz, 1, ey, ez, ex, by_y, by_x};
   }
@@ -112,7 +119,7 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
     l = Runs<Off>{sy, sz, sx, px, pz, 1, ey, ez, ex, by_y, by_x};
   } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kWarps && ey * ez >= 32) {
     // Z continues Y in the source (and, as pz = px * ey, in shared memory).
-    l = Runs<Off>{sx, 0, sy, 1, 0, px, ex, 1, ey * ez, FastDiv{0, 0}, FastDiv{0, 0}};
+    l = Runs<Off>{sx, 0, sy, 1, 0, px, ex, 1, ey * ez, kSinglePlane, FastDiv{0, 0}};
   } else {
     l = Runs<Off>{sx, sz, sy, 1, pz, px, ex, ez, ey, by_x, by_y};
   }
@@ -229,50 +236,58 @@ __device__ __forceinline__ void RunElements(Off g, int s, int j, int len, Off gj
   if (j + 3 * kStep < len) elem(g + 3 * gs, s + 3 * ss);
 }
 
+// Runs taken kLanes lanes at a time: each warp step covers 32 / kLanes runs
+// of the flattened (a, b) order, and each lane group strides its run.  Short
+// runs get few lanes, so every lane handles several elements and the per-run
+// set-up is amortised; a warp access still covers whole 32-byte sectors.
+template <typename Off, int kG, int kLanes, typename ElemF>
+__device__ __forceinline__ void GroupRuns(const Runs<Off>& w, ElemF& elem) {
+  constexpr int kGroups = 32 / kLanes;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane % kLanes, group = lane / kLanes;
+  const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
+  const int runs = w.na * w.nb;
+  for (int r0 = warp * kGroups; r0 < runs; r0 += kWarps * kGroups) {
+    const int r = r0 + group;
+    if (r < runs) {
+      const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
+      const int a = r - b * w.na;
+      RunElements<Off, kG, kLanes>(a * w.ga + b * w.gb + sub * g1, a * w.sa + b * w.sb + sub * w.sj, sub, w.len,
+                                   w.gj, w.sj, elem);
+    }
+  }
+}
+
 // Walk every element of a phase's runs; elem(g, s) moves one element.  The
 // CTA's threads are spread so every warp has work:
-//   * na >= warps, len >= 32: a warp per run; warps stride a, then b, with
-//                             constant increments (no division per run);
-//   * len >= threads:         the whole CTA strides each run in turn;
-//   * len >= 32:              a warp per run over the flattened (a, b);
-//   * otherwise:              the runs are packed end to end and the threads
-//                             stride the sequence.
+//   * few runs of at least a CTA's length: the whole CTA strides each run;
+//   * runs of 8 or more: 8, 16 or 32 lanes per run (by length), see GroupRuns;
+//   * shorter runs:      packed end to end, the threads stride the sequence.
 template <typename Off, int kG, typename ElemF>
 __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
-  const int na = w.na, nb = w.nb, len = w.len;
-  if (len >= 32 && na >= kWarps) {
-    const Off gstep = kWarps * w.ga;
-    const int sstep = kWarps * w.sa;
-    for (int b = 0; b < nb; ++b) {
-      Off g = warp * w.ga + b * w.gb + lane * g1;
-      int s = warp * w.sa + b * w.sb + lane * w.sj;
-      for (int a = warp; a < na; a += kWarps, g += gstep, s += sstep) {
-        RunElements<Off, kG, 32>(g, s, lane, len, w.gj, w.sj, elem);
-      }
-    }
-  } else if (len >= kThreads) {
-    for (int b = 0; b < nb; ++b) {
-      for (int a = 0; a < na; ++a) {
+  const int tid = threadIdx.x;
+  const int len = w.len;
+  if (len >= kThreads && w.na * w.nb < kWarps) {
+    const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
+    for (int b = 0; b < w.nb; ++b) {
+      for (int a = 0; a < w.na; ++a) {
         RunElements<Off, kG, kThreads>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
                                        w.gj, w.sj, elem);
       }
     }
-  } else if (len >= 32) {
-    for (int r = warp; r < na * nb; r += kWarps) {
-      const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
-      const int a = r - b * na;
-      RunElements<Off, kG, 32>(a * w.ga + b * w.gb + lane * g1, a * w.sa + b * w.sb + lane * w.sj, lane, len,
-                               w.gj, w.sj, elem);
-    }
+  } else if (len > 128) {
+    GroupRuns<Off, kG, 32>(w, elem);
+  } else if (len > 64) {
+    GroupRuns<Off, kG, 16>(w, elem);
+  } else if (len >= 8) {
+    GroupRuns<Off, kG, 8>(w, elem);
   } else {
-    const int total = na * nb * len;
+    const int total = w.na * w.nb * len;
     for (int f = tid; f < total; f += kThreads) {
       const int r = static_cast<int>(w.by_len.Div(static_cast<uint32_t>(f)));
       const int j = f - r * len;
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
-      const int a = r - b * na;
+      const int a = r - b * w.na;
       elem(a * w.ga + b * w.gb + j * w.gj, a * w.sa + b * w.sb + j * w.sj);
     }
   }
@@ -320,22 +335,37 @@ __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Of
   }
 }
 
+// Thread 0 only: advance the tile cursor (record, batch, tile within the
+// batch) to the next tile and decode it.
+template <typename E, typename Off>
+__device__ __forceinline__ void DecodeNext(const MapArgs& args, int64_t* cursor, TileState<Off>& next) {
+  int64_t rec = cursor[0], batch = cursor[1], local = cursor[2] + 1;
+  if (local == args.tiles_per_batch) { local = 0; ++batch; rec = 0; }
+  while (rec + 1 < args.nrec && args.recs[rec + 1].tile_begin <= local) ++rec;
+  cursor[0] = rec; cursor[1] = batch; cursor[2] = local;
+  DecodeTile<Off>(args, rec, batch, local, next);
+  E::Fetch(args, next.slot, next.batch, next.coef);
+}
+
 // One persistent CTA walks a contiguous range of tiles.  Per tile: issue the
 // asynchronous loads, let thread 0 decode the next tile while they fly, wait,
 // then write the destination runs out of shared memory.
 template <int Op, typename T, typename CA, typename CB, typename Off>
-__global__ void __launch_bounds__(kThreads, 4) MapKernel(MapArgs args) {
+__global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArgs args) {
   using E = Emit<Op, T, CA, CB>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ TileState<Off> states[2];        // the current tile and the next one
   __shared__ int64_t cursor[3];               // decoding thread: record, batch, tile within the batch
-  T* tile = reinterpret_cast<T*>(smem_raw);
-  T* base_tile = tile + args.tile_elems;      // update: destination base values, same layout
+  const T* tile = reinterpret_cast<const T*>(smem_raw);
+  const T* base_tile = tile + args.tile_elems;   // update: destination base values, same layout
+  const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  const uint32_t base_s = tile_s + static_cast<uint32_t>(args.tile_elems * sizeof(T));
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * per_cta;
   const int64_t count = first < total ? min(total, first + per_cta) - first : 0;
-  if (threadIdx.x == 0 && count > 0) {
+  if (count == 0) return;
+  if (threadIdx.x == 0) {
     const int64_t batch = first / args.tiles_per_batch;
     const int64_t local = first - batch * args.tiles_per_batch;
     int64_t lo = 0, hi = args.nrec - 1;
@@ -350,18 +380,9 @@ __global__ void __launch_bounds__(kThreads, 4) MapKernel(MapArgs args) {
   __syncthreads();
   for (int64_t i = 0; i < count; ++i) {
     const TileState<Off>& st = states[i & 1];
-    LoadTile<E, T, Off>(args, st, static_cast<uint32_t>(__cvta_generic_to_shared(tile)),
-                        static_cast<uint32_t>(__cvta_generic_to_shared(base_tile)));
+    LoadTile<E, T, Off>(args, st, tile_s, base_s);
     // While the copies fly, the decoding thread prepares the next tile.
-    if (threadIdx.x == 0 && i + 1 < count) {
-      int64_t rec = cursor[0], batch = cursor[1], local = cursor[2] + 1;
-      if (local == args.tiles_per_batch) { local = 0; ++batch; rec = 0; }
-      while (rec + 1 < args.nrec && args.recs[rec + 1].tile_begin <= local) ++rec;
-      cursor[0] = rec; cursor[1] = batch; cursor[2] = local;
-      TileState<Off>& next = states[(i + 1) & 1];
-      DecodeTile<Off>(args, rec, batch, local, next);
-      E::Fetch(args, next.slot, next.batch, next.coef);
-    }
+    if (threadIdx.x == 0 && i + 1 < count) DecodeNext<E, Off>(args, cursor, states[(i + 1) & 1]);
     WaitAsync();
     __syncthreads();
     // Store: destination runs out of the tile, with the rule specialised per kind.
@@ -522,13 +543,22 @@ int SmCount() {
 template <int Op, typename T, typename CA, typename CB, typename Off>
 void LaunchMapKernel(const MapArgs& args, int smem, cudaStream_t stream) {
   auto kernel = MapKernel<Op, T, CA, CB, Off>;
-  static int per_sm = [&] {
-    Check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024), "map attribute");
-    return 0;
+  // Allow as much dynamic shared memory as the device gives one block beyond
+  // the kernel's static shared memory.
+  static const bool configured = [&] {
+    int device = 0, limit = 48 * 1024;
+    cudaFuncAttributes attributes{};
+    Check(cudaGetDevice(&device), "map device");
+    Check(cudaDeviceGetAttribute(&limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device), "map shared limit");
+    Check(cudaFuncGetAttributes(&attributes, kernel), "map attributes");
+    Check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               limit - static_cast<int>(attributes.sharedSizeBytes)), "map attribute");
+    return true;
   }();
+  (void)configured;
   int blocks = 0;
   Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, smem), "map occupancy");
-  per_sm = std::max(blocks, 1);
+  const int per_sm = std::max(blocks, 1);
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t grid = std::min<int64_t>(total, static_cast<int64_t>(per_sm) * SmCount());
   kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
@@ -568,7 +598,12 @@ void WithStorage(int32_t dtype, F&& f) {
 }  // namespace
 
 void Check(cudaError_t status, const char* what) {
-  if (status != cudaSuccess) throw std::runtime_error(std::string("CUDA ") + what + ": " + cudaGetErrorString(status));
+  if (status != cudaSuccess) {
+    // Clear the runtime's last-error slot so the next launch check does not
+    // report this (non-sticky) failure again.
+    (void)cudaGetLastError();
+    throw std::runtime_error(std::string("CUDA ") + what + ": " + cudaGetErrorString(status));
+  }
 }
 
 void MapTileElements(const MapRecord* recs, int64_t count, int64_t* tile, int64_t* box) {

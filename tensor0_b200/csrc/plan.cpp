@@ -19,8 +19,11 @@ constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap 
 
 // Bytes of shared memory one map tile may stage (before row padding).  Update
 // tiles also stage the destination's base values, so they get half.
-constexpr int64_t kTileBytes = 32768;
-constexpr int64_t kUpdateTileBytes = 16384;
+#ifndef T0B_TILE_BYTES
+#define T0B_TILE_BYTES 32768
+#endif
+constexpr int64_t kTileBytes = T0B_TILE_BYTES;
+constexpr int64_t kUpdateTileBytes = T0B_TILE_BYTES / 2;
 
 // Split records so every axis extent fits in int32 and at most kMaxRank axes remain.
 std::vector<Record> SplitForDevice(const Record& record) {
