@@ -17,7 +17,7 @@
 struct t0b_plan {
   t0b::Plan plan;
   int map_smem = 0;        // dynamic shared memory of one map CTA (bytes)
-  int64_t tile_elems = 0;  // staged-tile elements; update plans place the base buffer after them
+  int64_t tile_elems = 0;  // source-stage elements; update plans place the base stage after them
 };
 
 namespace {
@@ -82,6 +82,14 @@ void Disjoint(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes) 
   const auto x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
   const bool overlap = x <= y ? y - x < a_bytes : x - y < b_bytes;
   if (overlap) throw t0b::InvalidArgument("input and output buffers overlap");
+}
+
+// Storage buffers are aligned to their element size, so the map engine's
+// 16-byte units of a run start on 16-byte boundaries.
+void RequireAligned(const void* buffer, int element_bytes, const char* what) {
+  if (buffer != nullptr && reinterpret_cast<uintptr_t>(buffer) % static_cast<uintptr_t>(element_bytes) != 0) {
+    throw t0b::InvalidArgument(std::string(what) + " buffer is not aligned to its element size");
+  }
 }
 
 const t0b::TableHeader& Header(const t0b_plan* plan) {
@@ -166,6 +174,8 @@ void Sum(const t0b_plan* plan, int32_t operation, int32_t dtype, const void* sou
   const uint64_t scratch_bytes = Bytes(b * p.scratch, eb);
   if (b != 0 && p.output_size != 0 && output == nullptr) throw t0b::InvalidArgument("output buffer is null");
   if (b != 0 && p.source_size != 0 && source == nullptr) throw t0b::InvalidArgument("source buffer is null");
+  RequireAligned(source, eb, "source");
+  RequireAligned(output, eb, "output");
   Disjoint(source, src_bytes, output, out_bytes);
   const size_t table_bytes = p.table.size() * sizeof(int64_t);
   if (table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
@@ -220,12 +230,12 @@ int t0b_plan_create(int32_t operation, const int64_t* words, size_t word_count,
     built->plan = t0b::BuildPlan(operation, words, word_count, coefficient_records, coefficient_count,
                                  element_bytes, flags);
     const auto& h = *reinterpret_cast<const t0b::TableHeader*>(built->plan.table.data());
-    int64_t tile = 0, box = 0;
-    t0b::MapTileElements(reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset),
-                         h.map_records, &tile, &box);
-    // Update plans also stage the destination's base values, in the tile's layout.
+    int64_t tile = 0, base = 0;
+    t0b::MapStageElements(reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset),
+                          h.map_records, element_bytes, &tile, &base);
+    // Update plans also stage the destination's base values.
     built->tile_elems = tile;
-    built->map_smem = static_cast<int>((operation == T0B_OP_UPDATE ? 2 * tile : tile) * element_bytes);
+    built->map_smem = static_cast<int>((operation == T0B_OP_UPDATE ? tile + base : tile) * element_bytes);
     *plan = built.release();
     g_created.fetch_add(1, std::memory_order_relaxed);
   });
@@ -271,6 +281,8 @@ int t0b_copy(const t0b_plan* plan, int32_t dtype, const void* source, void* outp
     if (b != 0 && p.output_size != 0 && output == nullptr) throw t0b::InvalidArgument("output buffer is null");
     if (b != 0 && p.source_size != 0 && source == nullptr) throw t0b::InvalidArgument("source buffer is null");
     if (device_table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+    RequireAligned(source, p.element_bytes, "source");
+    RequireAligned(output, p.element_bytes, "output");
     Disjoint(source, src_bytes, output, out_bytes);
     Disjoint(device_table, p.table.size() * sizeof(int64_t), output, out_bytes);
     if (b == 0 || p.output_size == 0) return;
@@ -317,6 +329,9 @@ int t0b_update(const t0b_plan* plan, int32_t dtype, const void* source, const vo
     }
     if (b != 0 && p.source_size != 0 && source == nullptr) throw t0b::InvalidArgument("source buffer is null");
     if (device_table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+    RequireAligned(source, eb, "source");
+    RequireAligned(base, eb, "base");
+    RequireAligned(output, eb, "output");
     if (alpha == nullptr || beta == nullptr) throw t0b::InvalidArgument("update coefficient buffer is null");
     const int ab = CoefficientBytes(alpha_dtype, dtype);
     const int bb = CoefficientBytes(beta_dtype, dtype);
