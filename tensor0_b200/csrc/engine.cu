@@ -321,45 +321,33 @@ __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Of
   }
 }
 
-// This lane's elements x0 + k, k = 0, kLanes, 2 kLanes, ... below ex of one
-// destination row, in blocks of eight predicated slots; slot(k) moves one.
-template <int kLanes, typename F>
-__device__ __forceinline__ void RowSlots(int x0, int ex, F&& slot) {
-  for (int k0 = 0; x0 + k0 < ex; k0 += 8 * kLanes) {
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      if (x0 + k0 + m * kLanes < ex) slot(k0 + m * kLanes);
-    }
-  }
-}
-
 // Write one tile: destination rows (y, z) along X, lane groups sized to ex
 // (or the whole CTA for few long rows).  Element (x, y, z) is read from its
 // source row -- row x (+ ex * z), column y (+ ey * z) for a transpose tile;
 // row y + ey * z, column x for a direct one -- plus that run's delta.  A
 // lane's columns step by its group size, a multiple of the 16-byte unit, so
-// its delta is fixed along the row.
-template <int K, typename E, typename T, typename Off>
+// its delta is fixed along the row.  A lane handles its columns in blocks of
+// eight slots without branches: a slot past the row end reads the lane's
+// first column again and skips only its store.  Values of a stage the tile
+// did not load (zero alpha or beta) are read but ignored by the element rule.
+template <int K, bool kUnitDx, typename E, typename T, typename Off>
 __device__ __forceinline__ void StoreTile(const MapArgs& args, const TileState<Off>& st, const E& emit,
                                           const T* tile, const T* base_tile) {
   constexpr int kVec = 16 / sizeof(T);
   constexpr uint32_t kMask = kVec - 1;
   const int ex = st.ex, ey = st.ey, rows = ey * st.ez;
-  const bool skip = emit.SkipSource();
-  const bool needs_base = E::kReadsBase && emit.NeedsBase();
   const bool direct = st.mode == kDirect, linear = st.linear;
   const int py = st.py, qx = st.qx;
-  const Off dx = st.dx, dy = st.dy, dz = st.dz;
+  const Off dx = kUnitDx ? Off{1} : st.dx, dy = st.dy, dz = st.dz;
   const FastDiv by_y = st.by_y;
   // Deltas of the source runs (zero for runs staged element by element).
   const bool src_units = (direct ? st.sx : st.sy) == 1;
   const uint32_t s0 = static_cast<uint32_t>(UnitOffset(static_cast<const T*>(args.src) + st.so));
   const uint32_t sx = static_cast<uint32_t>(st.sx), sy = static_cast<uint32_t>(st.sy), sz = static_cast<uint32_t>(st.sz);
-  const bool base_units = dx == 1;
   const uint32_t b0 = E::kReadsBase ? static_cast<uint32_t>(UnitOffset(static_cast<const T*>(args.base) + st.dof)) : 0u;
   const uint32_t udy = static_cast<uint32_t>(dy), udz = static_cast<uint32_t>(dz);
   T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
-  // Row r = y + ey * z as seen by the lane whose first column is x0.
+  // Row r = y + ey * z as seen by the lane whose first column is x0 < ex.
   auto row = [&](int r, int x0, auto lanes) {
     constexpr int kLanes = decltype(lanes)::value;
     const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
@@ -378,19 +366,30 @@ __device__ __forceinline__ void StoreTile(const MapArgs& args, const TileState<O
       t = (x0 + ex * z) * py + delta + y;
       t_step = py;
     }
-    const int b = needs_base ? r * qx + (base_units ? static_cast<int>((b0 + y * udy + z * udz) & kMask) : 0) + x0 : 0;
+    const T* tp = tile + t;
+    const T* bp = base_tile;
+    if constexpr (E::kReadsBase) {
+      bp += r * qx + (kUnitDx ? static_cast<int>((b0 + y * udy + z * udz) & kMask) : 0) + x0;
+    }
     T* p = out + (y * dy + z * dz + x0 * dx);
-    RowSlots<kLanes>(x0, ex, [&](int k) {
-      T v{}, old{};
-      if (!skip) v = tile[t + k * t_step];
-      if constexpr (E::kReadsBase) {
-        if (needs_base) old = base_tile[b + k];
+    for (int k0 = 0; x0 + k0 < ex; k0 += 8 * kLanes) {
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int k = k0 + m * kLanes;
+        const bool ok = x0 + k < ex;
+        const int kk = ok ? k : 0;
+        const T v = tp[kk * t_step];
+        T old{};
+        if constexpr (E::kReadsBase) old = bp[kk];
+        const T w = emit.template Apply<K>(v, old);
+        if (ok) p[kUnitDx ? k : k * dx] = w;
       }
-      p[k * dx] = emit.template Apply<K>(v, old);
-    });
+    }
   };
   auto groups = [&](auto lanes) {
-    ForRowGroups<decltype(lanes)::value>(rows, [&](int r, int sub) { row(r, sub, lanes); });
+    ForRowGroups<decltype(lanes)::value>(rows, [&](int r, int sub) {
+      if (sub < ex) row(r, sub, lanes);
+    });
   };
   if (rows < kWarps && ex >= kThreads) {
     for (int r = 0; r < rows; ++r) row(r, threadIdx.x, std::integral_constant<int, kThreads>{});
@@ -455,11 +454,16 @@ __global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArg
     __syncthreads();
     {
       const E emit(st.coef);
-      switch (emit.Kind()) {
-        case 1: StoreTile<1, E, T, Off>(args, st, emit, tile, base_tile); break;
-        case 2: StoreTile<2, E, T, Off>(args, st, emit, tile, base_tile); break;
-        default: StoreTile<0, E, T, Off>(args, st, emit, tile, base_tile); break;
-      }
+      auto store = [&](auto unit_dx) {
+        constexpr bool kUnitDx = decltype(unit_dx)::value;
+        switch (emit.Kind()) {
+          case 1: StoreTile<1, kUnitDx, E, T, Off>(args, st, emit, tile, base_tile); break;
+          case 2: StoreTile<2, kUnitDx, E, T, Off>(args, st, emit, tile, base_tile); break;
+          default: StoreTile<0, kUnitDx, E, T, Off>(args, st, emit, tile, base_tile); break;
+        }
+      };
+      if (st.dx == 1) store(std::true_type{});
+      else store(std::false_type{});
     }
     __syncthreads();
   }
