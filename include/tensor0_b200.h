@@ -109,10 +109,7 @@ uint64_t t0b_plan_destroyed_count(void);
 /*
  * Storage buffers (source, output, base) must be aligned to their element
  * size (4, 8, 8 and 16 bytes for F32, F64, C64 and C128); execute calls reject
- * others with status 1.  The engine copies unit-stride runs as the 16-byte
- * units that cover them, which may read up to 15 bytes on either side of a
- * run but never outside the 16-byte units holding the run's first and last
- * elements.
+ * others with status 1.
  *
  * Copy: out[b, dst(i)] = src[b, src(i)], bit-preserving; outputs no record
  * writes are zero.  Replaces Tensor0StrideCudaCopy{F32,F64,C64,C128}V1

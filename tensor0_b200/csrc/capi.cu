@@ -17,7 +17,7 @@
 struct t0b_plan {
   t0b::Plan plan;
   int map_smem = 0;        // dynamic shared memory of one map CTA (bytes)
-  int64_t tile_elems = 0;  // source-stage elements; update plans place the base stage after them
+  int64_t tile_elems = 0;  // staged-tile elements; update plans place the base buffer after them
 };
 
 namespace {
@@ -84,8 +84,8 @@ void Disjoint(const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes) 
   if (overlap) throw t0b::InvalidArgument("input and output buffers overlap");
 }
 
-// Storage buffers are aligned to their element size, so the map engine's
-// 16-byte units of a run start on 16-byte boundaries.
+// Storage buffers are aligned to their element size: the map engine copies
+// whole elements asynchronously (16 bytes at a time for C128).
 void RequireAligned(const void* buffer, int element_bytes, const char* what) {
   if (buffer != nullptr && reinterpret_cast<uintptr_t>(buffer) % static_cast<uintptr_t>(element_bytes) != 0) {
     throw t0b::InvalidArgument(std::string(what) + " buffer is not aligned to its element size");
@@ -230,12 +230,12 @@ int t0b_plan_create(int32_t operation, const int64_t* words, size_t word_count,
     built->plan = t0b::BuildPlan(operation, words, word_count, coefficient_records, coefficient_count,
                                  element_bytes, flags);
     const auto& h = *reinterpret_cast<const t0b::TableHeader*>(built->plan.table.data());
-    int64_t tile = 0, base = 0;
-    t0b::MapStageElements(reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset),
-                          h.map_records, element_bytes, &tile, &base);
-    // Update plans also stage the destination's base values.
+    int64_t tile = 0, box = 0;
+    t0b::MapTileElements(reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset),
+                         h.map_records, &tile, &box);
+    // Update plans also stage the destination's base values, in the tile's layout.
     built->tile_elems = tile;
-    built->map_smem = static_cast<int>((operation == T0B_OP_UPDATE ? tile + base : tile) * element_bytes);
+    built->map_smem = static_cast<int>((operation == T0B_OP_UPDATE ? 2 * tile : tile) * element_bytes);
     *plan = built.release();
     g_created.fetch_add(1, std::memory_order_relaxed);
   });

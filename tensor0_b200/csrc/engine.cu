@@ -5,12 +5,13 @@
 // every batch; each CTA walks a contiguous range of tiles.  A tile is a box
 // over the record's destination-innermost axis X, its source-innermost axis Y
 // and one further axis Z.  One thread decodes the tile with host-computed
-// division constants.  The CTA copies the tile's source runs into shared
-// memory in source order, as the 16-byte units that cover each run (one
-// cp.async per four f32 elements), then writes the destination rows along X,
-// each lane group reading its column of the staged rows.  Reads and writes
-// are coalesced and no element costs more than its shared-memory read, its
-// store and an addition or two.
+// division constants into two run lists: the source runs (along Y, continued
+// by Z when Z follows Y in the source), copied asynchronously into a
+// destination-ordered shared-memory tile, and the destination runs (rows
+// along X, or whole (x, y) planes when they are contiguous on both sides),
+// written out of it.  Warps take runs with constant address increments and
+// lanes stride each run, so reads and writes are coalesced and an element
+// costs its memory instruction and an addition or two.
 #include "engine.h"
 
 #include "arith.cuh"
@@ -38,38 +39,39 @@ struct FastDiv {
 
 __device__ __forceinline__ FastDiv Division(const DivisionConstants& c) { return FastDiv{c.magic, c.shift}; }
 
-// "Division" by 2^31: every row index of a single-plane row list is in plane 0.
+// "Division" by 2^31: every run index of a single-plane run list is in plane 0.
 constexpr FastDiv kSinglePlane{0, 31};
 
+// The runs one phase of a tile copies: run (a, b), a in [0, na), b in
+// [0, nb), starts at global offset a * ga + b * gb and shared-memory index
+// a * sa + b * sb; its element j in [0, len) sits at + j * gj and + j * sj.
+template <typename Off>
+struct Runs {
+  Off ga, gb, gj;
+  int sa, sb, sj;
+  int na, nb, len;
+  FastDiv by_na;           // run index -> b
+  FastDiv by_len;          // element index -> run (packed short runs only)
+};
+
 // A decoded tile, shared by the CTA.  In-tile offsets use Off (int32 unless
-// the plan marked a record wide).
-//
-// Shared memory holds the tile in source order: one row per source run (a
-// transpose tile's (x, z) runs along Y, or its x runs along (Y, Z) when Z
-// continues Y; a direct tile's (y, z) runs along X), `py` elements apart.  A
-// unit-stride run is copied as the 16-byte units that cover it, so its first
-// element sits delta elements into its row, delta being the run's global
-// offset modulo 16 bytes.  The update's base values are staged the same way
-// in destination order: one row per destination (y, z) row, `qx` apart.
+// the plan marked a record wide).  Shared memory holds the tile in
+// destination order: element (x, y, z) at x + px * y + pz * z, px = ex | 1
+// (odd, so source runs, which step px, hit distinct banks) and pz = px * ey.
 template <typename Off>
 struct TileState {
   int64_t so, dof;        // element offsets of the tile origin, batch included
-  Off sx, sy, sz, dx, dy, dz;
-  int ex, ey, ez;         // tile extents (edge tiles are smaller)
-  int mode;               // kTranspose or kDirect
-  int linear;             // transpose: Z continues Y in the source (one run per x)
-  int py, qx;             // row pitches of the source and base stages
-  FastDiv by_x, by_y;     // by ex, by ey
+  Runs<Off> load;         // source runs into shared memory
+  Runs<Off> store;        // destination runs out of shared memory (also the update's base loads)
   int64_t batch;
   int slot;
   alignas(16) unsigned char coef[32];   // the tile's coefficients, fetched by the decoding thread
 };
 
 // Thread 0 only: decode tile `local` of record `rec` in `batch`.
-template <typename T, typename Off>
+template <typename Off>
 __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_t batch, int64_t local,
                                            TileState<Off>& s) {
-  constexpr int kVec = 16 / sizeof(T);
   const MapRecord& r = a.recs[rec];
   uint32_t q = static_cast<uint32_t>(local - r.tile_begin);
   uint32_t chunk[3];
@@ -97,16 +99,30 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   const int64_t x0 = static_cast<int64_t>(chunk[0]) * r.t[0], y0 = static_cast<int64_t>(chunk[1]) * r.t[1];
   s.so = so + x0 * r.s[0] + y0 * r.s[1] + z0 * r.s[2];
   s.dof = dof + x0 * r.d[0] + y0 * r.d[1] + z0 * r.d[2];
-  s.sx = static_cast<Off>(r.s[0]); s.sy = static_cast<Off>(r.s[1]); s.sz = static_cast<Off>(r.s[2]);
-  s.dx = static_cast<Off>(r.d[0]); s.dy = static_cast<Off>(r.d[1]); s.dz = static_cast<Off>(r.d[2]);
-  s.ex = ex; s.ey = ey; s.ez = ez;
-  s.mode = r.mode;
-  s.linear = r.mode == kTranspose && ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1];
-  const int run = r.mode == kDirect ? ex : (s.linear ? ey * ez : ey);
-  s.py = static_cast<int>(RowPitch(run, kVec));
-  s.qx = static_cast<int>(RowPitch(ex, kVec));
-  s.by_x = Division(r.div_extent[last_x ? 1 : 0]);
-  s.by_y = Division(r.div_extent[last_y ? 3 : 2]);
+  const Off sx = static_cast<Off>(r.s[0]), sy = static_cast<Off>(r.s[1]), sz = static_cast<Off>(r.s[2]);
+  const Off dx = static_cast<Off>(r.d[0]), dy = static_cast<Off>(r.d[1]), dz = static_cast<Off>(r.d[2]);
+  const int px = ex | 1, pz = px * ey;
+  const FastDiv by_x = Division(r.div_extent[last_x ? 1 : 0]);
+  const FastDiv by_y = Division(r.div_extent[last_y ? 3 : 2]);
+  // Destination: when (x, y) is contiguous on both sides (an odd ex needs no
+  // padding) each z plane is one run, else (y, z) rows of ex.
+  Runs<Off>& w = s.store;
+  if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kThreads) {
+    w = Runs<Off>{dz, 0, dx, pz, 0, 1, ez, 1, ex * ey, kSinglePlane, FastDiv{0, 0}};
+  } else {
+    w = Runs<Off>{dy, dz, dx, px, pz, 1, ey, ez, ex, by_y, by_x};
+  }
+  // Source.
+  Runs<Off>& l = s.load;
+  if (r.mode == kDirect) {
+    // X is innermost on both sides: the source runs are the destination rows.
+    l = Runs<Off>{sy, sz, sx, px, pz, 1, ey, ez, ex, by_y, by_x};
+  } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kWarps && ey * ez >= 32) {
+    // Z continues Y in the source (and, as pz = px * ey, in shared memory).
+    l = Runs<Off>{sx, 0, sy, 1, 0, px, ex, 1, ey * ez, kSinglePlane, FastDiv{0, 0}};
+  } else {
+    l = Runs<Off>{sx, sz, sy, 1, pz, px, ex, ez, ey, by_x, by_y};
+  }
   s.batch = batch;
   s.slot = r.coef_slot;
 }
@@ -198,9 +214,97 @@ struct Emit<kOpUpdate, T, CA, CB> {
   }
 };
 
-// Asynchronous global -> shared copy of Bytes (no register round trip).  The
-// copies are ordered against shared-memory reads by WaitAsync and the CTA
-// barrier that follows it.
+// This thread's elements j = first_j, first_j + kStep, ... of one run
+// (first_j < kStep).  The number of unrolled blocks is the same for every
+// thread of the warp, and the last up-to-four elements are predicated, so
+// lanes never split between the two paths.  kG is the global step when known
+// at compile time (1: unit stride, the usual case, so the unrolled copies
+// address with immediate offsets), or 0 for gj.
+template <typename Off, int kG, int kStep, typename ElemF>
+__device__ __forceinline__ void RunElements(Off g, int s, int j, int len, Off gj, int sj, ElemF& elem) {
+  const Off gs = kStep * (kG != 0 ? static_cast<Off>(kG) : gj);
+  const int ss = kStep * sj;
+  for (int block = len / (4 * kStep); block > 0; --block, j += 4 * kStep, g += 4 * gs, s += 4 * ss) {
+    elem(g, s);
+    elem(g + gs, s + ss);
+    elem(g + 2 * gs, s + 2 * ss);
+    elem(g + 3 * gs, s + 3 * ss);
+  }
+  if (j < len) elem(g, s);
+  if (j + kStep < len) elem(g + gs, s + ss);
+  if (j + 2 * kStep < len) elem(g + 2 * gs, s + 2 * ss);
+  if (j + 3 * kStep < len) elem(g + 3 * gs, s + 3 * ss);
+}
+
+// Runs taken kLanes lanes at a time: each warp step covers 32 / kLanes runs
+// of the flattened (a, b) order, and each lane group strides its run.  Short
+// runs get few lanes, so every lane handles several elements and the per-run
+// set-up is amortised; a warp access still covers whole 32-byte sectors.
+template <typename Off, int kG, int kLanes, typename ElemF>
+__device__ __forceinline__ void GroupRuns(const Runs<Off>& w, ElemF& elem) {
+  constexpr int kGroups = 32 / kLanes;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane % kLanes, group = lane / kLanes;
+  const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
+  const int runs = w.na * w.nb;
+  for (int r0 = warp * kGroups; r0 < runs; r0 += kWarps * kGroups) {
+    const int r = r0 + group;
+    if (r < runs) {
+      const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
+      const int a = r - b * w.na;
+      RunElements<Off, kG, kLanes>(a * w.ga + b * w.gb + sub * g1, a * w.sa + b * w.sb + sub * w.sj, sub, w.len,
+                                   w.gj, w.sj, elem);
+    }
+  }
+}
+
+// Walk every element of a phase's runs; elem(g, s) moves one element.  The
+// CTA's threads are spread so every warp has work:
+//   * few runs of at least a CTA's length: the whole CTA strides each run;
+//   * runs of 8 or more: 8, 16 or 32 lanes per run (by length), see GroupRuns;
+//   * shorter runs:      packed end to end, the threads stride the sequence.
+template <typename Off, int kG, typename ElemF>
+__device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
+  const int tid = threadIdx.x;
+  const int len = w.len;
+  if (len >= kThreads && w.na * w.nb < kWarps) {
+    const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
+    for (int b = 0; b < w.nb; ++b) {
+      for (int a = 0; a < w.na; ++a) {
+        RunElements<Off, kG, kThreads>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
+                                       w.gj, w.sj, elem);
+      }
+    }
+  } else if (len > 128) {
+    GroupRuns<Off, kG, 32>(w, elem);
+  } else if (len > 64) {
+    GroupRuns<Off, kG, 16>(w, elem);
+  } else if (len >= 8) {
+    GroupRuns<Off, kG, 8>(w, elem);
+  } else {
+    const int total = w.na * w.nb * len;
+    for (int f = tid; f < total; f += kThreads) {
+      const int r = static_cast<int>(w.by_len.Div(static_cast<uint32_t>(f)));
+      const int j = f - r * len;
+      const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
+      const int a = r - b * w.na;
+      elem(a * w.ga + b * w.gb + j * w.gj, a * w.sa + b * w.sb + j * w.sj);
+    }
+  }
+}
+
+// `runs` lives in shared memory; the walk uses a register copy, which stores
+// through generic pointers cannot alias.
+template <typename Off, typename ElemF>
+__device__ __forceinline__ void Walk(const Runs<Off>& runs, ElemF&& elem) {
+  const Runs<Off> w = runs;
+  if (w.gj == 1) WalkRuns<Off, 1>(w, elem);
+  else WalkRuns<Off, 0>(w, elem);
+}
+
+// Asynchronous global -> shared copy of one element (no register round trip).
+// The copies are ordered against shared-memory reads by WaitAsync and the
+// CTA barrier that follows it.
 template <int Bytes>
 __device__ __forceinline__ void CopyAsync(uint32_t smem, const void* gmem) {
   if constexpr (Bytes == 16) {
@@ -212,211 +316,40 @@ __device__ __forceinline__ void CopyAsync(uint32_t smem, const void* gmem) {
 
 __device__ __forceinline__ void WaitAsync() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
-// Rows r = 0 .. rows - 1 handed out kLanes lanes at a time: each warp step
-// covers 32 / kLanes rows; f(r, sub) runs in the row's lane group, sub being
-// the lane's index in it.
-template <int kLanes, typename F>
-__device__ __forceinline__ void ForRowGroups(int rows, F&& f) {
-  constexpr int kGroups = 32 / kLanes;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int sub = lane % kLanes, group = lane / kLanes;
-  for (int r0 = warp * kGroups; r0 < rows; r0 += kWarps * kGroups) {
-    if (r0 + group < rows) f(r0 + group, sub);
-  }
-}
-
-// Element offset of a pointer modulo the 16-byte unit.
-template <typename T>
-__device__ __forceinline__ int UnitOffset(const T* p) {
-  return static_cast<int>((reinterpret_cast<uintptr_t>(p) / sizeof(T)) & (16 / sizeof(T) - 1));
-}
-
-// Stage `rows` runs of `len` elements into shared-memory rows `pitch` apart:
-// run r = a + na * b starts at from + a * ga + b * gb and steps gj.  A
-// unit-step run is copied as the 16-byte units covering it (its first element
-// lands UnitOffset(run) into the row; the units reach at most 15 bytes beyond
-// the run on either side, never past the 16-byte units holding its ends);
-// other runs element by element, from the row start.  Few long runs are
-// spread over the whole CTA, the rest over 4- to 32-lane groups.
-template <typename T, typename Off>
-__device__ __forceinline__ void StageRows(const T* from, int rows, int na, FastDiv by_na, Off ga, Off gb, Off gj,
-                                          int len, int pitch, uint32_t smem) {
-  constexpr int kVec = 16 / sizeof(T);
-  auto run_of = [&](int r) {
-    const int b = static_cast<int>(by_na.Div(static_cast<uint32_t>(r)));
-    const int a = r - b * na;
-    return from + (a * ga + b * gb);
-  };
-  if (gj == 1) {
-    const int most = (len + 2 * kVec - 2) / kVec;   // 16-byte units a run may span
-    auto units = [&](auto lanes) {
-      constexpr int kLanes = decltype(lanes)::value;
-      ForRowGroups<kLanes>(rows, [&](int r, int sub) {
-        const T* run = run_of(r);
-        const int delta = UnitOffset(run);
-        const T* aligned = run - delta;
-        const int n = (delta + len + kVec - 1) / kVec;
-        const uint32_t row = smem + static_cast<uint32_t>(r * pitch) * static_cast<uint32_t>(sizeof(T));
-        for (int u = sub; u < n; u += kLanes) CopyAsync<16>(row + 16 * u, aligned + kVec * u);
-      });
-    };
-    if (rows < kWarps && most >= kThreads) {
-      for (int r = 0; r < rows; ++r) {
-        const T* run = run_of(r);
-        const int delta = UnitOffset(run);
-        const T* aligned = run - delta;
-        const int n = (delta + len + kVec - 1) / kVec;
-        const uint32_t row = smem + static_cast<uint32_t>(r * pitch) * static_cast<uint32_t>(sizeof(T));
-        for (int u = threadIdx.x; u < n; u += kThreads) CopyAsync<16>(row + 16 * u, aligned + kVec * u);
-      }
-    } else if (most <= 4) {
-      units(std::integral_constant<int, 4>{});
-    } else if (most <= 8) {
-      units(std::integral_constant<int, 8>{});
-    } else if (most <= 16) {
-      units(std::integral_constant<int, 16>{});
-    } else {
-      units(std::integral_constant<int, 32>{});
-    }
-  } else {
-    auto elements = [&](auto lanes) {
-      constexpr int kLanes = decltype(lanes)::value;
-      ForRowGroups<kLanes>(rows, [&](int r, int sub) {
-        const T* run = run_of(r);
-        const uint32_t row = smem + static_cast<uint32_t>(r * pitch) * static_cast<uint32_t>(sizeof(T));
-        for (int j = sub; j < len; j += kLanes) {
-          CopyAsync<sizeof(T)>(row + static_cast<uint32_t>(j) * static_cast<uint32_t>(sizeof(T)), run + j * gj);
-        }
-      });
-    };
-    if (len <= 8) elements(std::integral_constant<int, 8>{});
-    else if (len <= 64) elements(std::integral_constant<int, 16>{});
-    else elements(std::integral_constant<int, 32>{});
-  }
-}
-
-// Issue the asynchronous loads of one tile: the source runs into the source
-// stage and, for update, the destination rows' base values into the base
-// stage.
+// Issue the asynchronous loads of one tile: the source runs into the tile
+// and, for update, the destination's base values into the same positions of
+// the base buffer.
 template <typename E, typename T, typename Off>
 __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Off>& st, uint32_t tile_s,
                                          uint32_t base_s) {
   const E emit(st.coef);
-  const int ex = st.ex, ey = st.ey, ez = st.ez;
   if (!emit.SkipSource()) {
-    const T* src = static_cast<const T*>(args.src) + st.so;
-    if (st.mode == kDirect) {
-      StageRows<T, Off>(src, ey * ez, ey, st.by_y, st.sy, st.sz, st.sx, ex, st.py, tile_s);
-    } else if (st.linear) {
-      StageRows<T, Off>(src, ex, ex, kSinglePlane, st.sx, Off{0}, st.sy, ey * ez, st.py, tile_s);
-    } else {
-      StageRows<T, Off>(src, ex * ez, ex, st.by_x, st.sx, st.sz, st.sy, ey, st.py, tile_s);
-    }
+    const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
+    Walk<Off>(st.load, [&](Off g, int s) { CopyAsync<sizeof(T)>(tile_s + s * static_cast<int>(sizeof(T)), src + g); });
   }
   if constexpr (E::kReadsBase) {
     if (emit.NeedsBase()) {
-      const T* base = static_cast<const T*>(args.base) + st.dof;
-      StageRows<T, Off>(base, ey * ez, ey, st.by_y, st.dy, st.dz, st.dx, ex, st.qx, base_s);
+      const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
+      Walk<Off>(st.store, [&](Off g, int s) { CopyAsync<sizeof(T)>(base_s + s * static_cast<int>(sizeof(T)), base + g); });
     }
-  }
-}
-
-// Write one tile: destination rows (y, z) along X, lane groups sized to ex
-// (or the whole CTA for few long rows).  Element (x, y, z) is read from its
-// source row -- row x (+ ex * z), column y (+ ey * z) for a transpose tile;
-// row y + ey * z, column x for a direct one -- plus that run's delta.  A
-// lane's columns step by its group size, a multiple of the 16-byte unit, so
-// its delta is fixed along the row.  A lane handles its columns in blocks of
-// eight slots without branches: a slot past the row end reads the lane's
-// first column again and skips only its store.  Values of a stage the tile
-// did not load (zero alpha or beta) are read but ignored by the element rule.
-template <int K, bool kUnitDx, typename E, typename T, typename Off>
-__device__ __forceinline__ void StoreTile(const MapArgs& args, const TileState<Off>& st, const E& emit,
-                                          const T* tile, const T* base_tile) {
-  constexpr int kVec = 16 / sizeof(T);
-  constexpr uint32_t kMask = kVec - 1;
-  const int ex = st.ex, ey = st.ey, rows = ey * st.ez;
-  const bool direct = st.mode == kDirect, linear = st.linear;
-  const int py = st.py, qx = st.qx;
-  const Off dx = kUnitDx ? Off{1} : st.dx, dy = st.dy, dz = st.dz;
-  const FastDiv by_y = st.by_y;
-  // Deltas of the source runs (zero for runs staged element by element).
-  const bool src_units = (direct ? st.sx : st.sy) == 1;
-  const uint32_t s0 = static_cast<uint32_t>(UnitOffset(static_cast<const T*>(args.src) + st.so));
-  const uint32_t sx = static_cast<uint32_t>(st.sx), sy = static_cast<uint32_t>(st.sy), sz = static_cast<uint32_t>(st.sz);
-  const uint32_t b0 = E::kReadsBase ? static_cast<uint32_t>(UnitOffset(static_cast<const T*>(args.base) + st.dof)) : 0u;
-  const uint32_t udy = static_cast<uint32_t>(dy), udz = static_cast<uint32_t>(dz);
-  T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
-  // Row r = y + ey * z as seen by the lane whose first column is x0 < ex.
-  auto row = [&](int r, int x0, auto lanes) {
-    constexpr int kLanes = decltype(lanes)::value;
-    const int z = static_cast<int>(by_y.Div(static_cast<uint32_t>(r)));
-    const int y = r - z * ey;
-    int t, t_step;
-    if (direct) {
-      const int delta = src_units ? static_cast<int>((s0 + y * sy + z * sz) & kMask) : 0;
-      t = r * py + delta + x0;
-      t_step = 1;
-    } else if (linear) {
-      const int delta = src_units ? static_cast<int>((s0 + x0 * sx) & kMask) : 0;
-      t = x0 * py + delta + r;
-      t_step = py;
-    } else {
-      const int delta = src_units ? static_cast<int>((s0 + x0 * sx + z * sz) & kMask) : 0;
-      t = (x0 + ex * z) * py + delta + y;
-      t_step = py;
-    }
-    const T* tp = tile + t;
-    const T* bp = base_tile;
-    if constexpr (E::kReadsBase) {
-      bp += r * qx + (kUnitDx ? static_cast<int>((b0 + y * udy + z * udz) & kMask) : 0) + x0;
-    }
-    T* p = out + (y * dy + z * dz + x0 * dx);
-    for (int k0 = 0; x0 + k0 < ex; k0 += 8 * kLanes) {
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int k = k0 + m * kLanes;
-        const bool ok = x0 + k < ex;
-        const int kk = ok ? k : 0;
-        const T v = tp[kk * t_step];
-        T old{};
-        if constexpr (E::kReadsBase) old = bp[kk];
-        const T w = emit.template Apply<K>(v, old);
-        if (ok) p[kUnitDx ? k : k * dx] = w;
-      }
-    }
-  };
-  auto groups = [&](auto lanes) {
-    ForRowGroups<decltype(lanes)::value>(rows, [&](int r, int sub) {
-      if (sub < ex) row(r, sub, lanes);
-    });
-  };
-  if (rows < kWarps && ex >= kThreads) {
-    for (int r = 0; r < rows; ++r) row(r, threadIdx.x, std::integral_constant<int, kThreads>{});
-  } else if (ex <= 64) {
-    groups(std::integral_constant<int, 8>{});
-  } else if (ex <= 128) {
-    groups(std::integral_constant<int, 16>{});
-  } else {
-    groups(std::integral_constant<int, 32>{});
   }
 }
 
 // Thread 0 only: advance the tile cursor (record, batch, tile within the
 // batch) to the next tile and decode it.
-template <typename E, typename T, typename Off>
+template <typename E, typename Off>
 __device__ __forceinline__ void DecodeNext(const MapArgs& args, int64_t* cursor, TileState<Off>& next) {
   int64_t rec = cursor[0], batch = cursor[1], local = cursor[2] + 1;
   if (local == args.tiles_per_batch) { local = 0; ++batch; rec = 0; }
   while (rec + 1 < args.nrec && args.recs[rec + 1].tile_begin <= local) ++rec;
   cursor[0] = rec; cursor[1] = batch; cursor[2] = local;
-  DecodeTile<T, Off>(args, rec, batch, local, next);
+  DecodeTile<Off>(args, rec, batch, local, next);
   E::Fetch(args, next.slot, next.batch, next.coef);
 }
 
 // One persistent CTA walks a contiguous range of tiles.  Per tile: issue the
 // asynchronous loads, let thread 0 decode the next tile while they fly, wait,
-// then write the destination rows out of shared memory.
+// then write the destination runs out of shared memory.
 template <int Op, typename T, typename CA, typename CB, typename Off>
 __global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArgs args) {
   using E = Emit<Op, T, CA, CB>;
@@ -424,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArg
   __shared__ TileState<Off> states[2];        // the current tile and the next one
   __shared__ int64_t cursor[3];               // decoding thread: record, batch, tile within the batch
   const T* tile = reinterpret_cast<const T*>(smem_raw);
-  const T* base_tile = tile + args.tile_elems;   // update: destination base values
+  const T* base_tile = tile + args.tile_elems;   // update: destination base values, same layout
   const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
   const uint32_t base_s = tile_s + static_cast<uint32_t>(args.tile_elems * sizeof(T));
   const int64_t total = args.tiles_per_batch * args.batches;
@@ -441,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArg
       if (args.recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
     }
     cursor[0] = lo; cursor[1] = batch; cursor[2] = local;
-    DecodeTile<T, Off>(args, lo, batch, local, states[0]);
+    DecodeTile<Off>(args, lo, batch, local, states[0]);
     E::Fetch(args, states[0].slot, states[0].batch, states[0].coef);
   }
   __syncthreads();
@@ -449,21 +382,31 @@ __global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArg
     const TileState<Off>& st = states[i & 1];
     LoadTile<E, T, Off>(args, st, tile_s, base_s);
     // While the copies fly, the decoding thread prepares the next tile.
-    if (threadIdx.x == 0 && i + 1 < count) DecodeNext<E, T, Off>(args, cursor, states[(i + 1) & 1]);
+    if (threadIdx.x == 0 && i + 1 < count) DecodeNext<E, Off>(args, cursor, states[(i + 1) & 1]);
     WaitAsync();
     __syncthreads();
+    // Store: destination runs out of the tile, with the rule specialised per kind.
     {
       const E emit(st.coef);
-      auto store = [&](auto unit_dx) {
-        constexpr bool kUnitDx = decltype(unit_dx)::value;
-        switch (emit.Kind()) {
-          case 1: StoreTile<1, kUnitDx, E, T, Off>(args, st, emit, tile, base_tile); break;
-          case 2: StoreTile<2, kUnitDx, E, T, Off>(args, st, emit, tile, base_tile); break;
-          default: StoreTile<0, kUnitDx, E, T, Off>(args, st, emit, tile, base_tile); break;
-        }
+      const bool skip = emit.SkipSource();
+      const bool needs_base = E::kReadsBase && emit.NeedsBase();
+      T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
+      auto store = [&](auto kind) {
+        constexpr int K = decltype(kind)::value;
+        Walk<Off>(st.store, [&](Off g, int s) {
+          T v{}, old{};
+          if (!skip) v = tile[s];
+          if constexpr (E::kReadsBase) {
+            if (needs_base) old = base_tile[s];
+          }
+          out[g] = emit.template Apply<K>(v, old);
+        });
       };
-      if (st.dx == 1) store(std::true_type{});
-      else store(std::false_type{});
+      switch (emit.Kind()) {
+        case 1: store(std::integral_constant<int, 1>{}); break;
+        case 2: store(std::integral_constant<int, 2>{}); break;
+        default: store(std::integral_constant<int, 0>{}); break;
+      }
     }
     __syncthreads();
   }
@@ -663,20 +606,14 @@ void Check(cudaError_t status, const char* what) {
   }
 }
 
-void MapStageElements(const MapRecord* recs, int64_t count, int32_t element_bytes, int64_t* tile, int64_t* base) {
-  const int64_t vec = 16 / element_bytes;
+void MapTileElements(const MapRecord* recs, int64_t count, int64_t* tile, int64_t* box) {
   *tile = 0;
-  *base = 0;
+  *box = 0;
   for (int64_t i = 0; i < count; ++i) {
     const int64_t t0 = recs[i].t[0], t1 = recs[i].t[1], t2 = recs[i].t[2];
-    const int64_t rows_of_x = t1 * t2 * RowPitch(t0, vec);
-    const int64_t need = recs[i].mode == kDirect
-                             ? rows_of_x
-                             : std::max(t0 * t2 * RowPitch(t1, vec), t0 * RowPitch(t1 * t2, vec));
-    *tile = std::max(*tile, need);
-    *base = std::max(*base, rows_of_x);
+    *tile = std::max<int64_t>(*tile, (t0 | 1) * t1 * t2);
+    *box = std::max<int64_t>(*box, t0 * t1 * t2);
   }
-  *tile = (*tile + vec - 1) / vec * vec;   // the base stage starts on a 16-byte boundary
 }
 
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,

@@ -27,7 +27,7 @@ struct MapArgs {
   void* out;
   int64_t src_size;
   int64_t out_size;
-  int64_t tile_elems;  // shared-memory elements of the source stage (the base stage follows)
+  int64_t tile_elems;  // shared-memory elements of the staged tile (the base buffer follows)
   const void* ca;      // accumulation: coefficient rows; update: alpha
   int64_t ca_count;
   const void* cb;      // update: beta
@@ -56,10 +56,8 @@ extern std::atomic<uint64_t> g_kernel_launches;
 // Throw std::runtime_error for a failed CUDA runtime call.
 void Check(cudaError_t status, const char* what);
 
-// Shared-memory elements of the largest source stage and of the largest base
-// stage (update) over a plan's records; the source stage is a whole number of
-// 16-byte units.
-void MapStageElements(const MapRecord* recs, int64_t count, int32_t element_bytes, int64_t* tile, int64_t* base);
+// Largest padded tile (shared-memory elements) and largest tile box over a plan's records.
+void MapTileElements(const MapRecord* recs, int64_t count, int64_t* tile, int64_t* box);
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
                int smem, bool wide, cudaStream_t stream);
 void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream);

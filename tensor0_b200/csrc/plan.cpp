@@ -139,10 +139,7 @@ void SetDivisions(MapRecord& r) {
   }
 }
 
-// Tile extents for a budget of staged shared-memory elements: a transpose
-// tile stages t0 * t2 source rows of t1 (or t0 rows of t1 * t2), a direct tile
-// t1 * t2 rows of t0, each at RowPitch (vec = elements per 16 bytes).
-MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int64_t vec, int64_t tile_begin) {
+MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int64_t tile_begin) {
   MapRecord out{};
   out.src_off = record.src_off;
   out.dst_off = record.dst_off;
@@ -203,23 +200,18 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int6
     z_axis = pick;
     rest.erase(std::find(rest.begin(), rest.end(), pick));
   }
-  if (z_axis != rank) put(2, z_axis);
   if (x == y) {
-    // Runs along X on both sides, one per (y, z); at most 1024 long, so a
-    // tile has several of them.
     out.mode = kDirect;
-    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], 1024));
+    out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], budget));   // one run per (y, z)
     out.t[1] = 1;
-    out.t[2] = static_cast<int32_t>(std::min<int64_t>(out.n[2], std::max<int64_t>(1, budget / RowPitch(out.t[0], vec))));
   } else {
     out.mode = kTranspose;
     put(1, y);
     out.t[0] = static_cast<int32_t>(std::min<int64_t>(out.n[0], 64));
-    out.t[1] = static_cast<int32_t>(std::min<int64_t>(out.n[1], 64));
-    while (out.t[1] > 1 && out.t[0] * RowPitch(out.t[1], vec) > budget) --out.t[1];
-    out.t[2] = static_cast<int32_t>(std::min<int64_t>(
-        out.n[2], std::max<int64_t>(1, budget / (int64_t{out.t[0]} * RowPitch(out.t[1], vec)))));
+    out.t[1] = static_cast<int32_t>(std::min<int64_t>(out.n[1], std::max<int64_t>(1, std::min<int64_t>(64, budget / out.t[0]))));
   }
+  if (z_axis != rank) put(2, z_axis);
+  out.t[2] = static_cast<int32_t>(std::min<int64_t>(out.n[2], std::max<int64_t>(1, budget / (int64_t{out.t[0]} * out.t[1]))));
   for (int i = 0; i < 3; ++i) out.c[i] = static_cast<int32_t>(CeilDiv(out.n[i], out.t[i]));
   out.nouter = static_cast<int32_t>(rest.size());
   for (std::size_t i = 0; i < rest.size(); ++i) put(3 + static_cast<int>(i), rest[i]);
@@ -376,8 +368,7 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     Record fused = records[i];
     Canonicalize(fused, true);
     MapRecord record = MakeMapRecord(fused, record_slot[i],
-                                     (operation == 1 ? kUpdateTileBytes : kTileBytes) / element_bytes,
-                                     16 / element_bytes, tiles);
+                                     (operation == 1 ? kUpdateTileBytes : kTileBytes) / element_bytes, tiles);
     tiles += MapTiles(record);
     plan.map_wide = plan.map_wide || NeedsWideOffsets(record);
     covered += ElementCount(records[i]);

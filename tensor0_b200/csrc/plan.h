@@ -41,22 +41,6 @@ inline DivisionConstants MakeDivision(uint32_t divisor) {
   return DivisionConstants{static_cast<uint32_t>(magic), shift};
 }
 
-#if defined(__CUDACC__)
-#define T0B_HOST_DEVICE __host__ __device__
-#else
-#define T0B_HOST_DEVICE
-#endif
-
-// Shared-memory pitch (elements) of a staged row of `len` elements whose
-// first element sits up to vec - 1 elements past a 16-byte boundary (vec =
-// elements per 16 bytes): room for the row's aligned 16-byte units, and an odd
-// number of units, so lanes that step whole rows fall in distinct banks.
-T0B_HOST_DEVICE inline int64_t RowPitch(int64_t len, int64_t vec) {
-  int64_t pitch = (len + 2 * vec - 2) / vec * vec;
-  if ((pitch / vec) % 2 == 0) pitch += vec;
-  return pitch;
-}
-
 // Map-engine record (device layout; shared by host and device code).
 struct alignas(16) MapRecord {
   int64_t src_off;
