@@ -126,6 +126,27 @@ def test_overlapping_buffers_are_rejected(lib):
     assert status == 1 and b"overlap" in err.value
 
 
+def test_misaligned_buffers_are_rejected(lib):
+    """Storage buffers must be aligned to their element size (checked before any launch)."""
+    words = np.asarray([1, 4, 4, 1, 1, 0, 0, 4, 1, 1])
+    err = _native.error_buffer()
+    table = ctypes.c_void_p(0x20000)
+    copy = stride.Plan(_native.OP_COPY, words, element_bytes=4)
+    status = lib.t0b_copy(copy._handle, _native.F32, ctypes.c_void_p(0x1002), ctypes.c_void_p(0x3000), 1,
+                          table, None, err, len(err))
+    assert status == 1 and b"source buffer is not aligned" in err.value
+    wide = stride.Plan(_native.OP_COPY, words, element_bytes=16)
+    status = lib.t0b_copy(wide._handle, _native.C128, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x3008), 1,
+                          table, None, err, len(err))
+    assert status == 1 and b"output buffer is not aligned" in err.value
+    update = stride.Plan(_native.OP_UPDATE, words, element_bytes=8)
+    alpha = ctypes.c_void_p(0x5000)
+    status = lib.t0b_update(update._handle, _native.F64, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x3004),
+                            ctypes.c_void_p(0x4000), 1, alpha, _native.F64, 1, alpha, _native.F64, 1,
+                            table, None, err, len(err))
+    assert status == 1 and b"base buffer is not aligned" in err.value
+
+
 def test_map_tiling_covers_every_element(lib):
     """The packed table's tiles account for every element of every record."""
     from tensor0_b200.structure import U1Irrep, hom, space
