@@ -27,6 +27,11 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+#ifndef T0B_MAP_THREADS
+#define T0B_MAP_THREADS 256   // threads of one map CTA
+#endif
+constexpr int kMapThreads = T0B_MAP_THREADS;
+constexpr int kMapWarps = kMapThreads / 32;
 #ifndef T0B_MAP_MIN_BLOCKS
 #define T0B_MAP_MIN_BLOCKS 4   // map CTAs per SM the register budget is sized for
 #endif
@@ -107,7 +112,7 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   // Destination: when (x, y) is contiguous on both sides (an odd ex needs no
   // padding) each z plane is one run, else (y, z) rows of ex.
   Runs<Off>& w = s.store;
-  if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kThreads) {
+  if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kMapThreads) {
     w = Runs<Off>{dz, 0, dx, pz, 0, 1, ez, 1, ex * ey, kSinglePlane, FastDiv{0, 0}};
   } else {
     w = Runs<Off>{dy, dz, dx, px, pz, 1, ey, ez, ex, by_y, by_x};
@@ -117,7 +122,7 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   if (r.mode == kDirect) {
     // X is innermost on both sides: the source runs are the destination rows.
     l = Runs<Off>{sy, sz, sx, px, pz, 1, ey, ez, ex, by_y, by_x};
-  } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kWarps && ey * ez >= 32) {
+  } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kMapWarps && ey * ez >= 32) {
     // Z continues Y in the source (and, as pz = px * ey, in shared memory).
     l = Runs<Off>{sx, 0, sy, 1, 0, px, ex, 1, ey * ez, kSinglePlane, FastDiv{0, 0}};
   } else {
@@ -247,7 +252,7 @@ __device__ __forceinline__ void GroupRuns(const Runs<Off>& w, ElemF& elem) {
   const int sub = lane % kLanes, group = lane / kLanes;
   const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
   const int runs = w.na * w.nb;
-  for (int r0 = warp * kGroups; r0 < runs; r0 += kWarps * kGroups) {
+  for (int r0 = warp * kGroups; r0 < runs; r0 += kMapWarps * kGroups) {
     const int r = r0 + group;
     if (r < runs) {
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
@@ -267,11 +272,11 @@ template <typename Off, int kG, typename ElemF>
 __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
   const int tid = threadIdx.x;
   const int len = w.len;
-  if (len >= kThreads && w.na * w.nb < kWarps) {
+  if (len >= kMapThreads && w.na * w.nb < kMapWarps) {
     const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
     for (int b = 0; b < w.nb; ++b) {
       for (int a = 0; a < w.na; ++a) {
-        RunElements<Off, kG, kThreads>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
+        RunElements<Off, kG, kMapThreads>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
                                        w.gj, w.sj, elem);
       }
     }
@@ -283,7 +288,7 @@ __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
     GroupRuns<Off, kG, 8>(w, elem);
   } else {
     const int total = w.na * w.nb * len;
-    for (int f = tid; f < total; f += kThreads) {
+    for (int f = tid; f < total; f += kMapThreads) {
       const int r = static_cast<int>(w.by_len.Div(static_cast<uint32_t>(f)));
       const int j = f - r * len;
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
@@ -351,7 +356,7 @@ __device__ __forceinline__ void DecodeNext(const MapArgs& args, int64_t* cursor,
 // asynchronous loads, let thread 0 decode the next tile while they fly, wait,
 // then write the destination runs out of shared memory.
 template <int Op, typename T, typename CA, typename CB, typename Off>
-__global__ void __launch_bounds__(kThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArgs args) {
+__global__ void __launch_bounds__(kMapThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArgs args) {
   using E = Emit<Op, T, CA, CB>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ TileState<Off> states[2];        // the current tile and the next one
@@ -557,11 +562,11 @@ void LaunchMapKernel(const MapArgs& args, int smem, cudaStream_t stream) {
   }();
   (void)configured;
   int blocks = 0;
-  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, smem), "map occupancy");
+  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kMapThreads, smem), "map occupancy");
   const int per_sm = std::max(blocks, 1);
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t grid = std::min<int64_t>(total, static_cast<int64_t>(per_sm) * SmCount());
-  kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(args);
+  kernel<<<static_cast<unsigned>(grid), kMapThreads, smem, stream>>>(args);
   Check(cudaGetLastError(), "map launch");
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }

@@ -22,8 +22,11 @@ constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap 
 #ifndef T0B_TILE_BYTES
 #define T0B_TILE_BYTES 32768
 #endif
+#ifndef T0B_UPDATE_TILE_BYTES
+#define T0B_UPDATE_TILE_BYTES (T0B_TILE_BYTES / 2)
+#endif
 constexpr int64_t kTileBytes = T0B_TILE_BYTES;
-constexpr int64_t kUpdateTileBytes = T0B_TILE_BYTES / 2;
+constexpr int64_t kUpdateTileBytes = T0B_UPDATE_TILE_BYTES;
 
 // Split records so every axis extent fits in int32 and at most kMaxRank axes remain.
 std::vector<Record> SplitForDevice(const Record& record) {
