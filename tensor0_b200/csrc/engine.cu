@@ -27,13 +27,21 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-#ifndef T0B_MAP_THREADS
-#define T0B_MAP_THREADS 256   // threads of one map CTA
+// Map CTA shape per operation (threads, CTAs per SM the register budget is
+// sized for).  Copy and accumulation do best with small CTAs, whose barriers
+// span few warps; update, which stages two operands, with larger ones and more
+// registers.
+#ifndef T0B_PERMUTE_THREADS
+#define T0B_PERMUTE_THREADS 128
 #endif
-constexpr int kMapThreads = T0B_MAP_THREADS;
-constexpr int kMapWarps = kMapThreads / 32;
-#ifndef T0B_MAP_MIN_BLOCKS
-#define T0B_MAP_MIN_BLOCKS 4   // map CTAs per SM the register budget is sized for
+#ifndef T0B_PERMUTE_MIN_BLOCKS
+#define T0B_PERMUTE_MIN_BLOCKS 8
+#endif
+#ifndef T0B_UPDATE_THREADS
+#define T0B_UPDATE_THREADS 256
+#endif
+#ifndef T0B_UPDATE_MIN_BLOCKS
+#define T0B_UPDATE_MIN_BLOCKS 3
 #endif
 
 // Division by a constant computed on the host (MakeDivision).
@@ -74,7 +82,7 @@ struct TileState {
 };
 
 // Thread 0 only: decode tile `local` of record `rec` in `batch`.
-template <typename Off>
+template <typename Off, int kThreadsPerCta>
 __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_t batch, int64_t local,
                                            TileState<Off>& s) {
   const MapRecord& r = a.recs[rec];
@@ -112,7 +120,7 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   // Destination: when (x, y) is contiguous on both sides (an odd ex needs no
   // padding) each z plane is one run, else (y, z) rows of ex.
   Runs<Off>& w = s.store;
-  if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kMapThreads) {
+  if (ey > 1 && px == ex && r.d[1] == static_cast<int64_t>(ex) * r.d[0] && ex * ey >= kThreadsPerCta) {
     w = Runs<Off>{dz, 0, dx, pz, 0, 1, ez, 1, ex * ey, kSinglePlane, FastDiv{0, 0}};
   } else {
     w = Runs<Off>{dy, dz, dx, px, pz, 1, ey, ez, ex, by_y, by_x};
@@ -122,7 +130,7 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   if (r.mode == kDirect) {
     // X is innermost on both sides: the source runs are the destination rows.
     l = Runs<Off>{sy, sz, sx, px, pz, 1, ey, ez, ex, by_y, by_x};
-  } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kMapWarps && ey * ez >= 32) {
+  } else if (ez > 1 && r.s[2] == static_cast<int64_t>(ey) * r.s[1] && ex >= kThreadsPerCta / 32 && ey * ez >= 32) {
     // Z continues Y in the source (and, as pz = px * ey, in shared memory).
     l = Runs<Off>{sx, 0, sy, 1, 0, px, ex, 1, ey * ez, kSinglePlane, FastDiv{0, 0}};
   } else {
@@ -245,14 +253,14 @@ __device__ __forceinline__ void RunElements(Off g, int s, int j, int len, Off gj
 // of the flattened (a, b) order, and each lane group strides its run.  Short
 // runs get few lanes, so every lane handles several elements and the per-run
 // set-up is amortised; a warp access still covers whole 32-byte sectors.
-template <typename Off, int kG, int kLanes, typename ElemF>
+template <typename Off, int kG, int kLanes, int kThreadsPerCta, typename ElemF>
 __device__ __forceinline__ void GroupRuns(const Runs<Off>& w, ElemF& elem) {
   constexpr int kGroups = 32 / kLanes;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane % kLanes, group = lane / kLanes;
   const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
   const int runs = w.na * w.nb;
-  for (int r0 = warp * kGroups; r0 < runs; r0 += kMapWarps * kGroups) {
+  for (int r0 = warp * kGroups; r0 < runs; r0 += (kThreadsPerCta / 32) * kGroups) {
     const int r = r0 + group;
     if (r < runs) {
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
@@ -268,27 +276,27 @@ __device__ __forceinline__ void GroupRuns(const Runs<Off>& w, ElemF& elem) {
 //   * few runs of at least a CTA's length: the whole CTA strides each run;
 //   * runs of 8 or more: 8, 16 or 32 lanes per run (by length), see GroupRuns;
 //   * shorter runs:      packed end to end, the threads stride the sequence.
-template <typename Off, int kG, typename ElemF>
+template <typename Off, int kG, int kThreadsPerCta, typename ElemF>
 __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
   const int tid = threadIdx.x;
   const int len = w.len;
-  if (len >= kMapThreads && w.na * w.nb < kMapWarps) {
+  if (len >= kThreadsPerCta && w.na * w.nb < kThreadsPerCta / 32) {
     const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
     for (int b = 0; b < w.nb; ++b) {
       for (int a = 0; a < w.na; ++a) {
-        RunElements<Off, kG, kMapThreads>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
+        RunElements<Off, kG, kThreadsPerCta>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
                                        w.gj, w.sj, elem);
       }
     }
   } else if (len > 128) {
-    GroupRuns<Off, kG, 32>(w, elem);
+    GroupRuns<Off, kG, 32, kThreadsPerCta>(w, elem);
   } else if (len > 64) {
-    GroupRuns<Off, kG, 16>(w, elem);
+    GroupRuns<Off, kG, 16, kThreadsPerCta>(w, elem);
   } else if (len >= 8) {
-    GroupRuns<Off, kG, 8>(w, elem);
+    GroupRuns<Off, kG, 8, kThreadsPerCta>(w, elem);
   } else {
     const int total = w.na * w.nb * len;
-    for (int f = tid; f < total; f += kMapThreads) {
+    for (int f = tid; f < total; f += kThreadsPerCta) {
       const int r = static_cast<int>(w.by_len.Div(static_cast<uint32_t>(f)));
       const int j = f - r * len;
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
@@ -300,11 +308,11 @@ __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
 
 // `runs` lives in shared memory; the walk uses a register copy, which stores
 // through generic pointers cannot alias.
-template <typename Off, typename ElemF>
+template <typename Off, int kThreadsPerCta, typename ElemF>
 __device__ __forceinline__ void Walk(const Runs<Off>& runs, ElemF&& elem) {
   const Runs<Off> w = runs;
-  if (w.gj == 1) WalkRuns<Off, 1>(w, elem);
-  else WalkRuns<Off, 0>(w, elem);
+  if (w.gj == 1) WalkRuns<Off, 1, kThreadsPerCta>(w, elem);
+  else WalkRuns<Off, 0, kThreadsPerCta>(w, elem);
 }
 
 // Asynchronous global -> shared copy of one element (no register round trip).
@@ -324,40 +332,47 @@ __device__ __forceinline__ void WaitAsync() { asm volatile("cp.async.wait_all;\n
 // Issue the asynchronous loads of one tile: the source runs into the tile
 // and, for update, the destination's base values into the same positions of
 // the base buffer.
-template <typename E, typename T, typename Off>
+template <typename E, typename T, typename Off, int kThreadsPerCta>
 __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Off>& st, uint32_t tile_s,
                                          uint32_t base_s) {
   const E emit(st.coef);
   if (!emit.SkipSource()) {
     const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
-    Walk<Off>(st.load, [&](Off g, int s) { CopyAsync<sizeof(T)>(tile_s + s * static_cast<int>(sizeof(T)), src + g); });
+    Walk<Off, kThreadsPerCta>(st.load, [&](Off g, int s) { CopyAsync<sizeof(T)>(tile_s + s * static_cast<int>(sizeof(T)), src + g); });
   }
   if constexpr (E::kReadsBase) {
     if (emit.NeedsBase()) {
       const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
-      Walk<Off>(st.store, [&](Off g, int s) { CopyAsync<sizeof(T)>(base_s + s * static_cast<int>(sizeof(T)), base + g); });
+      Walk<Off, kThreadsPerCta>(st.store, [&](Off g, int s) { CopyAsync<sizeof(T)>(base_s + s * static_cast<int>(sizeof(T)), base + g); });
     }
   }
 }
 
 // Thread 0 only: advance the tile cursor (record, batch, tile within the
 // batch) to the next tile and decode it.
-template <typename E, typename Off>
+template <typename E, typename Off, int kThreadsPerCta>
 __device__ __forceinline__ void DecodeNext(const MapArgs& args, int64_t* cursor, TileState<Off>& next) {
   int64_t rec = cursor[0], batch = cursor[1], local = cursor[2] + 1;
   if (local == args.tiles_per_batch) { local = 0; ++batch; rec = 0; }
   while (rec + 1 < args.nrec && args.recs[rec + 1].tile_begin <= local) ++rec;
   cursor[0] = rec; cursor[1] = batch; cursor[2] = local;
-  DecodeTile<Off>(args, rec, batch, local, next);
+  DecodeTile<Off, kThreadsPerCta>(args, rec, batch, local, next);
   E::Fetch(args, next.slot, next.batch, next.coef);
 }
 
 // One persistent CTA walks a contiguous range of tiles.  Per tile: issue the
 // asynchronous loads, let thread 0 decode the next tile while they fly, wait,
 // then write the destination runs out of shared memory.
+template <int Op>
+struct MapShape {
+  static constexpr int kThreads = Op == kOpUpdate ? T0B_UPDATE_THREADS : T0B_PERMUTE_THREADS;
+  static constexpr int kMinBlocks = Op == kOpUpdate ? T0B_UPDATE_MIN_BLOCKS : T0B_PERMUTE_MIN_BLOCKS;
+};
+
 template <int Op, typename T, typename CA, typename CB, typename Off>
-__global__ void __launch_bounds__(kMapThreads, T0B_MAP_MIN_BLOCKS) MapKernel(MapArgs args) {
+__global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBlocks) MapKernel(MapArgs args) {
   using E = Emit<Op, T, CA, CB>;
+  constexpr int kCta = MapShape<Op>::kThreads;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ TileState<Off> states[2];        // the current tile and the next one
   __shared__ int64_t cursor[3];               // decoding thread: record, batch, tile within the batch
@@ -379,15 +394,15 @@ __global__ void __launch_bounds__(kMapThreads, T0B_MAP_MIN_BLOCKS) MapKernel(Map
       if (args.recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
     }
     cursor[0] = lo; cursor[1] = batch; cursor[2] = local;
-    DecodeTile<Off>(args, lo, batch, local, states[0]);
+    DecodeTile<Off, kCta>(args, lo, batch, local, states[0]);
     E::Fetch(args, states[0].slot, states[0].batch, states[0].coef);
   }
   __syncthreads();
   for (int64_t i = 0; i < count; ++i) {
     const TileState<Off>& st = states[i & 1];
-    LoadTile<E, T, Off>(args, st, tile_s, base_s);
+    LoadTile<E, T, Off, kCta>(args, st, tile_s, base_s);
     // While the copies fly, the decoding thread prepares the next tile.
-    if (threadIdx.x == 0 && i + 1 < count) DecodeNext<E, Off>(args, cursor, states[(i + 1) & 1]);
+    if (threadIdx.x == 0 && i + 1 < count) DecodeNext<E, Off, kCta>(args, cursor, states[(i + 1) & 1]);
     WaitAsync();
     __syncthreads();
     // Store: destination runs out of the tile, with the rule specialised per kind.
@@ -398,7 +413,7 @@ __global__ void __launch_bounds__(kMapThreads, T0B_MAP_MIN_BLOCKS) MapKernel(Map
       T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
       auto store = [&](auto kind) {
         constexpr int K = decltype(kind)::value;
-        Walk<Off>(st.store, [&](Off g, int s) {
+        Walk<Off, kCta>(st.store, [&](Off g, int s) {
           T v{}, old{};
           if (!skip) v = tile[s];
           if constexpr (E::kReadsBase) {
@@ -562,11 +577,11 @@ void LaunchMapKernel(const MapArgs& args, int smem, cudaStream_t stream) {
   }();
   (void)configured;
   int blocks = 0;
-  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kMapThreads, smem), "map occupancy");
+  Check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, MapShape<Op>::kThreads, smem), "map occupancy");
   const int per_sm = std::max(blocks, 1);
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t grid = std::min<int64_t>(total, static_cast<int64_t>(per_sm) * SmCount());
-  kernel<<<static_cast<unsigned>(grid), kMapThreads, smem, stream>>>(args);
+  kernel<<<static_cast<unsigned>(grid), MapShape<Op>::kThreads, smem, stream>>>(args);
   Check(cudaGetLastError(), "map launch");
   g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
 }
