@@ -195,6 +195,64 @@ class ClockSampler:
                 "samples": len(self.samples), "source": "nvml, 10 ms"}
 
 
+DMRG_DEGENERACIES = [8, 18, 37, 68, 112, 166, 219, 259, 274, 259, 219, 166, 112, 68, 37, 18, 8]
+
+
+def contraction_bench(device, steps: int, warmup: int):
+    """DMRG environment contraction L . A in f64: chi = 2048 over U(1) charges -8..8
+    (degeneracies exp(-q^2 / 18) rounded to sum 2048), physical d = 2 {0, 1}, MPO
+    bond w = 5 (charge 0).  Times the whole tensorcontract (operand permutes plus
+    the grouped sector GEMM) and the sector GEMM launch alone, against an f64 cuBLAS
+    GEMM measured here (8192^3, best of 5)."""
+    import torch
+    from tensor0_b200 import stride
+    from tensor0_b200.structure import U1Irrep, degeneracy_structure, hom, space
+    from tensor0_b200.tensor_map import TensorMap, contract_plan, permute, tensorcontract
+    chi = space(U1Irrep, {q: d for q, d in zip(range(-8, 9), DMRG_DEGENERACIES)})
+    phys = space(U1Irrep, {0: 1, 1: 1})
+    w = space(U1Irrep, {0: 5})
+    a_space, l_space = hom((chi, phys), (chi,)), hom((chi,), (chi, w))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4)
+    a = TensorMap(a_space, torch.randn(degeneracy_structure(a_space).total_dim, generator=gen, device=device,
+                                       dtype=torch.float64))
+    l = TensorMap(l_space, torch.randn(degeneracy_structure(l_space).total_dim, generator=gen, device=device,
+                                       dtype=torch.float64))
+    axes, output = ((1,), (0,)), (((0, 0), (1, 1)), ((0, 2), (1, 2)))
+    plan = contract_plan(l_space, a_space, (1,), (0,), output)
+    flops = plan.gemm.flops_real
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, count):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(count):
+            fn()
+        end.record(stream)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / count
+
+    whole_ms = timed(lambda: tensorcontract(l, a, axes=axes, output=output), steps)
+    left, right = (a, l) if plan.reversed_operands else (l, a)
+    lcan, rcan = permute(left, plan.left_p).data, permute(right, plan.right_p).data
+    out = torch.empty(degeneracy_structure(plan.canonical).total_dim, dtype=torch.float64, device=device)
+    gemm_ms = timed(lambda: stride.sector_gemm(plan.gemm, lcan, rcan, out), steps)
+    x = torch.randn(8192, 8192, dtype=torch.float64, device=device)
+    y = torch.randn(8192, 8192, dtype=torch.float64, device=device)
+    cublas_ms = min(timed(lambda: torch.matmul(x, y), 1) for _ in range(5))
+    peak = 2 * 8192 ** 3 / (cublas_ms / 1e3) / 1e12
+    gemm_tf = flops / (gemm_ms / 1e3) / 1e12
+    return {"metric": "contraction TFLOP/s", "value": round(flops / (whole_ms / 1e3) / 1e12, 3), "unit": "TFLOP/s",
+            "dtype": "f64", "workload": "DMRG L.A, U1 chi=2048 (sigma=3), d=2, w=5", "sectors": plan.gemm.sectors,
+            "flops_per_step": flops, "ms_per_step": round(whole_ms, 4),
+            "gemm": {"kernel": "DmmaGemm (sector GEMM launch alone)", "value": round(gemm_tf, 3),
+                     "ms": round(gemm_ms, 4), "peak": round(peak, 2), "frac": round(gemm_tf / peak, 4),
+                     "peak_kind": "measured here: cuBLAS f64 GEMM 8192^3, best of 5"}}
+
+
 def device_uuid(index: int) -> str:
     import torch
     try:
@@ -364,6 +422,8 @@ def main():
         e_elapsed = float(t.item())
     e2e_value = world * step_bytes * e2e_steps / (e_elapsed / 1e3) / 1e9
 
+    contraction = contraction_bench(device, max(args.steps, 5), args.warmup) if rank == 0 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -388,6 +448,7 @@ def main():
                     "h2d_bytes_per_step": 2 * n * item, "d2h_bytes_per_step": 2 * n * item},
             "gpu_launches": int(launches),
             "clocks": clocks.summary(),
+            "contraction": contraction,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
