@@ -228,72 +228,83 @@ struct Emit<kOpUpdate, T, CA, CB> {
 };
 
 // This thread's elements j = first_j, first_j + kStep, ... of one run
-// (first_j < kStep).  The number of unrolled blocks is the same for every
-// thread of the warp, and the last up-to-four elements are predicated, so
-// lanes never split between the two paths.  kG is the global step when known
-// at compile time (1: unit stride, the usual case, so the unrolled copies
-// address with immediate offsets), or 0 for gj.
-template <typename Off, int kG, int kStep, typename ElemF>
-__device__ __forceinline__ void RunElements(Off g, int s, int j, int len, Off gj, int sj, ElemF& elem) {
+// (first_j < kStep): element j's global address is p + (j - first_j) * gj and
+// its shared-memory byte address s + (j - first_j) / kStep * ss.  The number
+// of unrolled blocks is the same for every thread of the warp, and the last
+// up-to-four elements are predicated, so lanes never split between the two
+// paths.  kG is the global step when known at compile time (1: unit stride,
+// the usual case) and kSs the shared-memory step of kStep elements (or 0 for
+// ss); known steps become immediate address offsets.
+template <typename P, typename Off, int kG, int kSs, int kStep, typename ElemF>
+__device__ __forceinline__ void RunElements(P p, uint32_t s, int j, int len, Off gj, uint32_t ss_runtime,
+                                            ElemF& elem) {
   const Off gs = kStep * (kG != 0 ? static_cast<Off>(kG) : gj);
-  const int ss = kStep * sj;
-  for (int block = len / (4 * kStep); block > 0; --block, j += 4 * kStep, g += 4 * gs, s += 4 * ss) {
-    elem(g, s);
-    elem(g + gs, s + ss);
-    elem(g + 2 * gs, s + 2 * ss);
-    elem(g + 3 * gs, s + 3 * ss);
+  const uint32_t ss = kSs != 0 ? static_cast<uint32_t>(kSs) : ss_runtime;
+  for (int block = len / (4 * kStep); block > 0; --block, j += 4 * kStep, p += 4 * gs, s += 4 * ss) {
+    elem(p, s);
+    elem(p + gs, s + ss);
+    elem(p + 2 * gs, s + 2 * ss);
+    elem(p + 3 * gs, s + 3 * ss);
   }
-  if (j < len) elem(g, s);
-  if (j + kStep < len) elem(g + gs, s + ss);
-  if (j + 2 * kStep < len) elem(g + 2 * gs, s + 2 * ss);
-  if (j + 3 * kStep < len) elem(g + 3 * gs, s + 3 * ss);
+  if (j < len) elem(p, s);
+  if (j + kStep < len) elem(p + gs, s + ss);
+  if (j + 2 * kStep < len) elem(p + 2 * gs, s + 2 * ss);
+  if (j + 3 * kStep < len) elem(p + 3 * gs, s + 3 * ss);
 }
 
 // Runs taken kLanes lanes at a time: each warp step covers 32 / kLanes runs
 // of the flattened (a, b) order, and each lane group strides its run.  Short
 // runs get few lanes, so every lane handles several elements and the per-run
 // set-up is amortised; a warp access still covers whole 32-byte sectors.
-template <typename Off, int kG, int kLanes, int kThreadsPerCta, typename ElemF>
-__device__ __forceinline__ void GroupRuns(const Runs<Off>& w, ElemF& elem) {
+// kSUnit: the run's shared-memory step is one element.
+template <typename P, typename Off, int kG, bool kSUnit, int kLanes, int kThreadsPerCta, typename ElemF>
+__device__ __forceinline__ void GroupRuns(const Runs<Off>& w, P base, uint32_t sbase, ElemF& elem) {
   constexpr int kGroups = 32 / kLanes;
+  constexpr uint32_t kBytes = sizeof(*base);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane % kLanes, group = lane / kLanes;
   const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
   const int runs = w.na * w.nb;
+  const uint32_t ss = static_cast<uint32_t>(kLanes * w.sj) * kBytes;
   for (int r0 = warp * kGroups; r0 < runs; r0 += (kThreadsPerCta / 32) * kGroups) {
     const int r = r0 + group;
     if (r < runs) {
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
       const int a = r - b * w.na;
-      RunElements<Off, kG, kLanes>(a * w.ga + b * w.gb + sub * g1, a * w.sa + b * w.sb + sub * w.sj, sub, w.len,
-                                   w.gj, w.sj, elem);
+      RunElements<P, Off, kG, kSUnit ? kLanes * kBytes : 0, kLanes>(
+          base + (a * w.ga + b * w.gb + sub * g1), sbase + static_cast<uint32_t>(a * w.sa + b * w.sb + sub * w.sj) * kBytes,
+          sub, w.len, w.gj, ss, elem);
     }
   }
 }
 
-// Walk every element of a phase's runs; elem(g, s) moves one element.  The
-// CTA's threads are spread so every warp has work:
+// Walk every element of a phase's runs; elem(p, s) moves the element at
+// global address p and shared-memory byte address s.  The CTA's threads are
+// spread so every warp has work:
 //   * few runs of at least a CTA's length: the whole CTA strides each run;
 //   * runs of 8 or more: 8, 16 or 32 lanes per run (by length), see GroupRuns;
 //   * shorter runs:      packed end to end, the threads stride the sequence.
-template <typename Off, int kG, int kThreadsPerCta, typename ElemF>
-__device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
+template <typename P, typename Off, int kG, bool kSUnit, int kThreadsPerCta, typename ElemF>
+__device__ __forceinline__ void WalkRuns(const Runs<Off>& w, P base, uint32_t sbase, ElemF& elem) {
+  constexpr uint32_t kBytes = sizeof(*base);
   const int tid = threadIdx.x;
   const int len = w.len;
   if (len >= kThreadsPerCta && w.na * w.nb < kThreadsPerCta / 32) {
     const Off g1 = kG != 0 ? static_cast<Off>(kG) : w.gj;
+    const uint32_t ss = static_cast<uint32_t>(kThreadsPerCta * w.sj) * kBytes;
     for (int b = 0; b < w.nb; ++b) {
       for (int a = 0; a < w.na; ++a) {
-        RunElements<Off, kG, kThreadsPerCta>(a * w.ga + b * w.gb + tid * g1, a * w.sa + b * w.sb + tid * w.sj, tid, len,
-                                       w.gj, w.sj, elem);
+        RunElements<P, Off, kG, kSUnit ? kThreadsPerCta * kBytes : 0, kThreadsPerCta>(
+            base + (a * w.ga + b * w.gb + tid * g1), sbase + static_cast<uint32_t>(a * w.sa + b * w.sb + tid * w.sj) * kBytes,
+            tid, len, w.gj, ss, elem);
       }
     }
   } else if (len > 128) {
-    GroupRuns<Off, kG, 32, kThreadsPerCta>(w, elem);
+    GroupRuns<P, Off, kG, kSUnit, 32, kThreadsPerCta>(w, base, sbase, elem);
   } else if (len > 64) {
-    GroupRuns<Off, kG, 16, kThreadsPerCta>(w, elem);
+    GroupRuns<P, Off, kG, kSUnit, 16, kThreadsPerCta>(w, base, sbase, elem);
   } else if (len >= 8) {
-    GroupRuns<Off, kG, 8, kThreadsPerCta>(w, elem);
+    GroupRuns<P, Off, kG, kSUnit, 8, kThreadsPerCta>(w, base, sbase, elem);
   } else {
     const int total = w.na * w.nb * len;
     for (int f = tid; f < total; f += kThreadsPerCta) {
@@ -301,18 +312,39 @@ __device__ __forceinline__ void WalkRuns(const Runs<Off>& w, ElemF& elem) {
       const int j = f - r * len;
       const int b = static_cast<int>(w.by_na.Div(static_cast<uint32_t>(r)));
       const int a = r - b * w.na;
-      elem(a * w.ga + b * w.gb + j * w.gj, a * w.sa + b * w.sb + j * w.sj);
+      elem(base + (a * w.ga + b * w.gb + j * w.gj), sbase + static_cast<uint32_t>(a * w.sa + b * w.sb + j * w.sj) * kBytes);
     }
   }
 }
 
 // `runs` lives in shared memory; the walk uses a register copy, which stores
 // through generic pointers cannot alias.
-template <typename Off, int kThreadsPerCta, typename ElemF>
-__device__ __forceinline__ void Walk(const Runs<Off>& runs, ElemF&& elem) {
+template <typename Off, int kThreadsPerCta, bool kSUnit, typename P, typename ElemF>
+__device__ __forceinline__ void Walk(const Runs<Off>& runs, P base, uint32_t sbase, ElemF&& elem) {
   const Runs<Off> w = runs;
-  if (w.gj == 1) WalkRuns<Off, 1, kThreadsPerCta>(w, elem);
-  else WalkRuns<Off, 0, kThreadsPerCta>(w, elem);
+  if (w.gj == 1) WalkRuns<P, Off, 1, kSUnit, kThreadsPerCta>(w, base, sbase, elem);
+  else WalkRuns<P, Off, 0, kSUnit, kThreadsPerCta>(w, base, sbase, elem);
+}
+
+// Shared-memory load of one element at a byte address.  Volatile, so it stays
+// after the CTA barrier that publishes the tile.
+template <typename T>
+__device__ __forceinline__ T LoadShared(uint32_t addr) {
+  T v;
+  if constexpr (sizeof(T) == 4) {
+    uint32_t x;
+    asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(x) : "r"(addr));
+    __builtin_memcpy(&v, &x, 4);
+  } else if constexpr (sizeof(T) == 8) {
+    uint2 x;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];\n" : "=r"(x.x), "=r"(x.y) : "r"(addr));
+    __builtin_memcpy(&v, &x, 8);
+  } else {
+    uint4 x;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w) : "r"(addr));
+    __builtin_memcpy(&v, &x, 16);
+  }
+  return v;
 }
 
 // Asynchronous global -> shared copy of one element (no register round trip).
@@ -336,15 +368,12 @@ template <typename E, typename T, typename Off, int kThreadsPerCta>
 __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Off>& st, uint32_t tile_s,
                                          uint32_t base_s) {
   const E emit(st.coef);
+  auto copy = [](const T* p, uint32_t s) { CopyAsync<sizeof(T)>(s, p); };
   if (!emit.SkipSource()) {
-    const T* __restrict__ src = static_cast<const T*>(args.src) + st.so;
-    Walk<Off, kThreadsPerCta>(st.load, [&](Off g, int s) { CopyAsync<sizeof(T)>(tile_s + s * static_cast<int>(sizeof(T)), src + g); });
+    Walk<Off, kThreadsPerCta, false>(st.load, static_cast<const T*>(args.src) + st.so, tile_s, copy);
   }
   if constexpr (E::kReadsBase) {
-    if (emit.NeedsBase()) {
-      const T* __restrict__ base = static_cast<const T*>(args.base) + st.dof;
-      Walk<Off, kThreadsPerCta>(st.store, [&](Off g, int s) { CopyAsync<sizeof(T)>(base_s + s * static_cast<int>(sizeof(T)), base + g); });
-    }
+    if (emit.NeedsBase()) Walk<Off, kThreadsPerCta, true>(st.store, static_cast<const T*>(args.base) + st.dof, base_s, copy);
   }
 }
 
@@ -376,8 +405,6 @@ __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBloc
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ TileState<Off> states[2];        // the current tile and the next one
   __shared__ int64_t cursor[3];               // decoding thread: record, batch, tile within the batch
-  const T* tile = reinterpret_cast<const T*>(smem_raw);
-  const T* base_tile = tile + args.tile_elems;   // update: destination base values, same layout
   const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
   const uint32_t base_s = tile_s + static_cast<uint32_t>(args.tile_elems * sizeof(T));
   const int64_t total = args.tiles_per_batch * args.batches;
@@ -411,15 +438,16 @@ __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBloc
       const bool skip = emit.SkipSource();
       const bool needs_base = E::kReadsBase && emit.NeedsBase();
       T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
+      const uint32_t base_offset = base_s - tile_s;
       auto store = [&](auto kind) {
         constexpr int K = decltype(kind)::value;
-        Walk<Off, kCta>(st.store, [&](Off g, int s) {
+        Walk<Off, kCta, true>(st.store, out, tile_s, [&](T* p, uint32_t s) {
           T v{}, old{};
-          if (!skip) v = tile[s];
+          if (!skip) v = LoadShared<T>(s);
           if constexpr (E::kReadsBase) {
-            if (needs_base) old = base_tile[s];
+            if (needs_base) old = LoadShared<T>(s + base_offset);
           }
-          out[g] = emit.template Apply<K>(v, old);
+          *p = emit.template Apply<K>(v, old);
         });
       };
       switch (emit.Kind()) {
