@@ -49,6 +49,7 @@ def parse():
     p.add_argument("--dtype", choices=("f32", "c64"), default="f32")
     p.add_argument("--e2e-steps", type=int, default=None, help="end-to-end steps (default: min(steps, 8))")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-contraction", action="store_true", help="skip the contraction TFLOP/s measurement")
     p.add_argument("--scale", type=int, default=64,
                    help="leg degeneracy scale (64 = the benchmark workload; smaller values for profiling)")
     return p.parse_args()
@@ -422,7 +423,9 @@ def main():
         e_elapsed = float(t.item())
     e2e_value = world * step_bytes * e2e_steps / (e_elapsed / 1e3) / 1e9
 
-    contraction = contraction_bench(device, max(args.steps, 5), args.warmup) if rank == 0 else None
+    contraction = None
+    if rank == 0 and not args.no_contraction:
+        contraction = contraction_bench(device, max(args.steps, 5), args.warmup)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
