@@ -18,14 +18,14 @@ constexpr uint64_t kExtentLimit = uint64_t{1} << 30;   // per-axis extent kept i
 constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap check
 
 // Bytes of shared memory one map tile may stage (before row padding): 16 KB
-// for copy and accumulation (eight 128-thread CTAs per SM), 24 KB for update,
+// for copy and accumulation (eight 128-thread CTAs per SM), 32 KB for update,
 // which stages the destination's base values beside it (three 256-thread CTAs
-// per SM).
+// per SM, 64 KB each).
 #ifndef T0B_TILE_BYTES
 #define T0B_TILE_BYTES 16384
 #endif
 #ifndef T0B_UPDATE_TILE_BYTES
-#define T0B_UPDATE_TILE_BYTES 24576
+#define T0B_UPDATE_TILE_BYTES 32768
 #endif
 constexpr int64_t kTileBytes = T0B_TILE_BYTES;
 constexpr int64_t kUpdateTileBytes = T0B_UPDATE_TILE_BYTES;
