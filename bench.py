@@ -62,7 +62,7 @@ def workload_space(scale: int = 64):
     return hom((v, v), (v, v)), degs
 
 
-def workload_config(args, elements: int = 1023777634):
+def workload_config(args, elements: int):
     return {"workload": "u1-4leg permute((2,0),(3,1)) + beta=1 accumulate",
             "legs": f"U1 q=-4..4, deg round({args.scale} exp(-q^2/8))", "elements": elements,
             "sub_blocks": 489, "dtype": args.dtype, "l2": "inputs larger than the 126 MB L2, no flush",
@@ -73,53 +73,60 @@ def workload_config(args, elements: int = 1023777634):
 # CPU: the reference's own executors on a bounded sample.
 
 
-SAMPLE_SCALE = 40     # degeneracies round(40 exp(-q^2/8)): same structure, ~1/6.6 of the elements
+SAMPLE_SCALE = 40     # degeneracies round(40 exp(-q^2/8)): same structure, ~1/6.8 of the elements
 
 
-def cpu_reference_steps(dtype_name: str, steps: int, warmup: int, threads: int):
-    """Time the compiled reference (oracle/_ref) on the sample workload; GB/s."""
+def cpu_reference_steps(dtype_name: str, steps: int, warmup: int, threads: int, scale: int):
+    """Time the compiled reference (oracle/_ref) on the workload at degeneracy
+    `scale`: instantiated once, then `warmup` untimed and `steps` timed
+    executions of the permute-accumulate and the beta = 1 update; GB/s."""
     from oracle import ref
     from tensor0_b200.structure import degeneracy_structure
     from tensor0_b200.tensor_map import permute_plan
-    h, degs = workload_space(SAMPLE_SCALE)
+    h, degs = workload_space(scale)
     plan = permute_plan(h, (2, 0), (3, 1))
     n = degeneracy_structure(h).total_dim
     dtype = np.float32 if dtype_name == "f32" else np.complex64
     rng = np.random.default_rng(7)
-    x = rng.standard_normal(n).astype(np.float32)
     if dtype == np.complex64:
-        x = (x + 1j * rng.standard_normal(n).astype(np.float32)).astype(np.complex64)
+        x = np.empty(n, np.complex64)
+        x.real = rng.standard_normal(n, dtype=np.float32)
+        x.imag = rng.standard_normal(n, dtype=np.float32)
+    else:
+        x = rng.standard_normal(n, dtype=np.float32)
     z = np.zeros(plan.output_size, dtype)
     y = np.empty(plan.output_size, dtype)
     records = np.arange(len(plan.transform.src))
     ones = [np.float32(1.0)] * len(records)
     ref.set_threads(threads)
+    accumulate = ref.Prepared(3, plan.words, records, outputs_disjoint=True)
+    update = ref.Prepared(1, plan.words)
     item = np.dtype(dtype).itemsize
     step_bytes = 5 * n * item
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        ref.accumulation(plan.words, x, plan.output_size, ones, records, outputs_disjoint=True, threads=threads,
-                         out=y)
-        ref.update(plan.words, x, z, np.float32(1.0), np.float32(1.0), threads=threads, out=z)
+        accumulate.accumulation(x, y, ones, threads=threads)
+        update.update(x, z, z, np.float32(1.0), np.float32(1.0), threads=threads)
         if i >= warmup:
             times.append(time.perf_counter() - t0)
     seconds = sum(times)
-    sample = (f"u1-4leg deg round({SAMPLE_SCALE} exp(-q^2/8)) {dict(degs)}, N={n} ({step_bytes / 1e9:.2f} GB "
-              f"algorithmic per step), {steps} steps")
-    return step_bytes * steps / seconds / 1e9, seconds * 1e3 / steps, sample
+    sample = (f"u1-4leg deg round({scale} exp(-q^2/8)) {dict(degs)}, N={n} ({step_bytes / 1e9:.2f} GB "
+              f"algorithmic per step), {steps} timed steps after {warmup} warm-up, instantiated once")
+    return step_bytes * steps / seconds / 1e9, seconds * 1e3 / steps, sample, n
 
 
 def run_reference(args, rank: int):
+    """The reference's CPU executors on the same workload as the GPU arm (full
+    size), on all host cores; rank 0 only."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    steps = max(1, min(args.steps, 10))
-    value, ms, sample = cpu_reference_steps(args.dtype, steps, max(1, min(args.warmup, 2)), threads)
-    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+    value, ms, sample, n = cpu_reference_steps(args.dtype, args.steps, args.warmup, threads, args.scale)
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": args.dtype, "data": "synthetic N(0,1), seeded",
-            "config": workload_config(args), "impl": "reference",
+            "config": workload_config(args, n), "impl": "reference",
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -430,7 +437,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        value_cpu, ms_cpu, sample = cpu_reference_steps(args.dtype, 3, 1, threads)
+        value_cpu, ms_cpu, sample, _ = cpu_reference_steps(args.dtype, 3, 1, threads, SAMPLE_SCALE)
         cpu = {"value": round(value_cpu, 3), "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample}
 
     if rank == 0:

@@ -55,6 +55,10 @@ extern "C" {
  * ffi/reduction_impl.h:193-200).  Without it the planner proves disjointness
  * itself or falls back to record-ordered execution. */
 #define T0B_PLAN_OUTPUTS_DISJOINT 1u
+/* Run the map engine with 64-bit in-tile offsets even when every record's
+ * strides fit 32 bits (the planner selects them by itself for records whose
+ * tile spans exceed 2^31 elements); results are identical. */
+#define T0B_PLAN_WIDE_OFFSETS 2u
 
 typedef struct t0b_plan t0b_plan;
 
@@ -156,7 +160,10 @@ int t0b_reduction(const t0b_plan* plan, int32_t dtype, const void* source, void*
  * Calls needing more than 16 MiB of scratch (batches * scratch elements *
  * element size) are rejected with status 1.  The first call on a device looks
  * up the array's device address with that device current; make that first
- * call before any stream capture.  Every call shares the one array per device:
+ * call before any stream capture.  The address is looked up again whenever
+ * the current CUDA context differs from the one it was found in; a primary
+ * context recreated by cudaDeviceReset may return under the same handle, so a
+ * device reset after the first call is not supported.  Every call shares the one array per device:
  * calls that overlap on the GPU (different streams, no ordering) race.  The
  * kernels write every partial they read, so nothing needs clearing between
  * calls.  Allocates nothing.
@@ -199,15 +206,20 @@ int t0b_axpby(int32_t dtype, int64_t n, double alpha_real, double alpha_imag, co
  * host_table / device_table: `sectors` rows of t0b_gemm_table_words(1) int64
  * words, built on the host by t0b_gemm_table_build from rows of 6 words
  * {m, n, k, a_off, b_off, c_off}; the caller copies the host words to device
- * memory it owns.  F64 and C128 run on the FP64 tensor cores (DMMA); F32 and
- * C64 accumulate in FP32.
+ * memory it owns.  left_size / right_size / output_size are the operands'
+ * lengths in elements: every row must address inside them, output blocks
+ * must be pairwise disjoint, the output must not overlap either input, and
+ * the operands must be aligned to their element size (16 bytes for C128);
+ * otherwise status 1 and nothing is launched.  F64 and C128 run on the FP64
+ * tensor cores (DMMA); F32 and C64 accumulate in FP32.
  */
 size_t t0b_gemm_table_words(int64_t sectors);
 int t0b_gemm_table_build(int64_t sectors, const int64_t* spec, int64_t* table, char* error,
                          size_t error_size);
 int t0b_sector_gemm(int32_t dtype, int64_t sectors, const int64_t* host_table,
-                    const int64_t* device_table, const void* left, const void* right,
-                    void* output, void* stream, char* error, size_t error_size);
+                    const int64_t* device_table, const void* left, int64_t left_size,
+                    const void* right, int64_t right_size, void* output, int64_t output_size,
+                    void* stream, char* error, size_t error_size);
 
 /* Number of kernels this library launched since load (for launch accounting). */
 uint64_t t0b_kernel_launches(void);

@@ -27,9 +27,16 @@ def available() -> bool:
     return LIBRARY.exists()
 
 
-def build(reference: str = "/root/reference") -> Path:
+def reference_root() -> str:
+    """Where the reference sources lie: $TENSOR0_REFERENCE, else the checkout
+    this build recipe was written against."""
+    return os.environ.get("TENSOR0_REFERENCE", "/root/reference")
+
+
+def build(reference: str | None = None) -> Path:
     """Compile the reference executors (only where the reference sources exist)."""
     import subprocess
+    reference = reference or reference_root()
     if not Path(reference).exists():
         raise RuntimeError("reference sources are not present; oracle/_ref cannot be rebuilt here")
     subprocess.run(["make", "-C", str(HERE), f"REFERENCE={reference}", f"-j{os.cpu_count() or 4}"], check=True)
@@ -154,3 +161,52 @@ def update(words, source: np.ndarray, base: np.ndarray, alpha, beta, threads: in
           ctypes.c_void_p(b.ctypes.data), ctypes.c_int(_DTYPES[b.dtype]), ctypes.c_int64(-1 if b.ndim == 0 else b.shape[0]),
           ctypes.c_int64(batches), ctypes.c_int64(threads))
     return out
+
+
+class Prepared:
+    """An instantiated accumulation (3) or update (1) call of the reference:
+    decode, validation and preparation run once here, so that `execute_*`
+    times execution alone, as one XLA executable reuses its prepared state."""
+
+    def __init__(self, operation: int, words, coefficient_records=(), outputs_disjoint: bool = False):
+        self._lib = lib()
+        self._lib.t0ref_prepare.restype = ctypes.c_void_p
+        self.words = _words(words)
+        self.records = _words(coefficient_records)
+        err = ctypes.create_string_buffer(512)
+        handle = self._lib.t0ref_prepare(ctypes.c_int32(operation), self.words.ctypes.data_as(c_i64p),
+                                         ctypes.c_size_t(self.words.size), self.records.ctypes.data_as(c_i64p),
+                                         ctypes.c_size_t(self.records.size), ctypes.c_int64(int(outputs_disjoint)),
+                                         err, ctypes.c_size_t(len(err)))
+        if not handle:
+            raise ReferenceError(1, err.value.decode(errors="replace"))
+        self._handle = ctypes.c_void_p(handle)
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle is not None and handle.value:
+            self._lib.t0ref_release(handle)
+            self._handle = None
+
+    def accumulation(self, source: np.ndarray, out: np.ndarray, coefficients=(), threads: int = 1) -> np.ndarray:
+        batches = int(np.prod(source.shape[:-1], dtype=np.int64))
+        _, arrays, pointers, dtypes, counts = _coefficients(list(coefficients), self.records)
+        _call(self._lib.t0ref_execute_accumulation, self._handle, ctypes.c_int(_DTYPES[source.dtype]), pointers,
+              dtypes, counts, ctypes.c_void_p(source.ctypes.data), ctypes.c_int64(source.shape[-1]),
+              ctypes.c_void_p(out.ctypes.data), ctypes.c_int64(out.shape[-1]), ctypes.c_int64(batches),
+              ctypes.c_int64(threads))
+        del arrays
+        return out
+
+    def update(self, source: np.ndarray, base: np.ndarray, out: np.ndarray, alpha, beta,
+               threads: int = 1) -> np.ndarray:
+        batches = int(np.prod(base.shape[:-1], dtype=np.int64))
+        a = np.ascontiguousarray(np.asarray(alpha))
+        b = np.ascontiguousarray(np.asarray(beta))
+        _call(self._lib.t0ref_execute_update, self._handle, ctypes.c_int(_DTYPES[base.dtype]),
+              ctypes.c_void_p(source.ctypes.data), ctypes.c_int64(source.shape[-1]), ctypes.c_void_p(base.ctypes.data),
+              ctypes.c_void_p(out.ctypes.data), ctypes.c_int64(base.shape[-1]), ctypes.c_void_p(a.ctypes.data),
+              ctypes.c_int(_DTYPES[a.dtype]), ctypes.c_int64(-1 if a.ndim == 0 else a.shape[0]),
+              ctypes.c_void_p(b.ctypes.data), ctypes.c_int(_DTYPES[b.dtype]),
+              ctypes.c_int64(-1 if b.ndim == 0 else b.shape[0]), ctypes.c_int64(batches), ctypes.c_int64(threads))
+        return out

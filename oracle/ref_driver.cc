@@ -8,9 +8,11 @@
 // reduction_impl.h}).  JAX is not available here, so this driver binds the
 // same handler templates directly with hand-built XLA_FFI_Buffer structs and
 // an XLA_FFI_Api whose thread pool is a real std::thread pool (the pattern of
-// tests/stride/native/cpp/thread_pool_test_support.h:9-40).  Every call runs
-// instantiate (descriptor decode, validation, sort/fuse preparation) and then
-// execute, exactly as one XLA executable would.
+// tests/stride/native/cpp/thread_pool_test_support.h:9-40).  The one-shot
+// calls run instantiate (descriptor decode, validation, sort/fuse preparation)
+// and then execute; the t0ref_prepare / t0ref_execute_* pair keeps the
+// instantiated state across executions, as one XLA executable does, so that
+// timing covers execution only.
 
 #define TENSOR0_STRIDE_TEST_NO_HANDLERS
 #include "ffi/reduction_impl.h"
@@ -22,6 +24,7 @@
 #include <cstring>
 #include <deque>
 #include <functional>
+#include <memory>
 #include <mutex>
 #include <optional>
 #include <thread>
@@ -296,6 +299,78 @@ int t0ref_update(int dtype, const int64_t* words, size_t word_count,
     auto b = MakeBuffer(beta_dtype, beta, beta_count < 0 ? 0 : 1, beta_count < 0 ? nullptr : beta_dims);
     auto future = native::Update<Dtype>({words, word_count}, prepared->get(), ffi::AnyBuffer(&input),
         ffi::BufferR2<Dtype>(&old), ffi::AnyBuffer(&a), ffi::AnyBuffer(&b),
+        ffi::BufferR2<Dtype>(&result), Pool(threads).Get());
+    return Wait(std::move(future), error, error_size);
+  });
+}
+
+// A prepared call: instantiated once, executed many times.
+struct t0ref_call {
+  int32_t operation = 0;          // 1 update, 3 accumulation
+  std::vector<int64_t> words;
+  std::vector<int64_t> records;
+  int64_t outputs_disjoint = 0;
+  std::unique_ptr<native::PreparedState> state;
+};
+
+t0ref_call* t0ref_prepare(int32_t operation, const int64_t* words, size_t word_count,
+                          const int64_t* coefficient_records, size_t coefficient_count,
+                          int64_t outputs_disjoint, char* error, size_t error_size) {
+  auto call = std::make_unique<t0ref_call>();
+  call->operation = operation;
+  call->words.assign(words, words + word_count);
+  call->records.assign(coefficient_records, coefficient_records + coefficient_count);
+  call->outputs_disjoint = outputs_disjoint;
+  const ffi::Span<const int64_t> layout(call->words.data(), call->words.size());
+  const ffi::Span<const int64_t> records(call->records.data(), call->records.size());
+  auto prepared = operation == 3 ? native::InstantiateAccumulation(layout, records, outputs_disjoint)
+                                 : native::InstantiatePrepared(layout);
+  if (!prepared.has_value()) {
+    Report(prepared.error(), error, error_size);
+    return nullptr;
+  }
+  call->state = std::move(*prepared);
+  return call.release();
+}
+
+void t0ref_release(t0ref_call* call) { delete call; }
+
+int t0ref_execute_accumulation(const t0ref_call* call, int dtype, const void* const* coefficient_data,
+                               const int* coefficient_dtypes, const int64_t* coefficient_counts,
+                               const void* source, int64_t source_size, void* output, int64_t output_size,
+                               int64_t batches, int64_t threads, char* error, size_t error_size) {
+  CoefficientArgs coefficients(call->records.size(), coefficient_data, coefficient_dtypes, coefficient_counts);
+  return DispatchStorage(dtype, [&](auto tag) {
+    constexpr auto Dtype = decltype(tag)::value;
+    int64_t source_dims[2] = {batches, source_size};
+    int64_t output_dims[2] = {batches, output_size};
+    auto input = MakeBuffer(dtype, source, 2, source_dims);
+    auto result = MakeBuffer(dtype, output, 2, output_dims);
+    auto future = native::Accumulation<Dtype>({call->words.data(), call->words.size()},
+        {call->records.data(), call->records.size()}, call->state.get(), ffi::AnyBuffer(&input),
+        ffi::RemainingArgs(&coefficients.args, 0), ffi::BufferR2<Dtype>(&result),
+        Pool(threads).Get(), call->outputs_disjoint);
+    return Wait(std::move(future), error, error_size);
+  });
+}
+
+int t0ref_execute_update(const t0ref_call* call, int dtype, const void* source, int64_t source_size,
+                         const void* base, void* output, int64_t output_size, const void* alpha,
+                         int alpha_dtype, int64_t alpha_count, const void* beta, int beta_dtype,
+                         int64_t beta_count, int64_t batches, int64_t threads, char* error, size_t error_size) {
+  return DispatchStorage(dtype, [&](auto tag) {
+    constexpr auto Dtype = decltype(tag)::value;
+    int64_t source_dims[2] = {batches, source_size};
+    int64_t output_dims[2] = {batches, output_size};
+    int64_t alpha_dims[1] = {alpha_count};
+    int64_t beta_dims[1] = {beta_count};
+    auto input = MakeBuffer(dtype, source, 2, source_dims);
+    auto old = MakeBuffer(dtype, base, 2, output_dims);
+    auto result = MakeBuffer(dtype, output, 2, output_dims);
+    auto a = MakeBuffer(alpha_dtype, alpha, alpha_count < 0 ? 0 : 1, alpha_count < 0 ? nullptr : alpha_dims);
+    auto b = MakeBuffer(beta_dtype, beta, beta_count < 0 ? 0 : 1, beta_count < 0 ? nullptr : beta_dims);
+    auto future = native::Update<Dtype>({call->words.data(), call->words.size()}, call->state.get(),
+        ffi::AnyBuffer(&input), ffi::BufferR2<Dtype>(&old), ffi::AnyBuffer(&a), ffi::AnyBuffer(&b),
         ffi::BufferR2<Dtype>(&result), Pool(threads).Get());
     return Wait(std::move(future), error, error_size);
   });

@@ -62,6 +62,24 @@ def addresses(shape, strides, offset) -> np.ndarray:
     return index.reshape(-1)
 
 
+def _view(array: np.ndarray, offset: int, shape, strides) -> np.ndarray:
+    """The strided box (offset, shape, element strides) of the last axis of
+    ``array`` as a numpy view, batch axes first.  The layout was validated, so
+    every address of the box lies inside the array."""
+    item = array.itemsize
+    batch_shape = array.shape[:-1]
+    batch_strides = array.strides[:-1]
+    flat = array.reshape(-1, array.shape[-1]) if batch_shape else array.reshape(1, -1)
+    base = flat[:, offset:] if array.shape[-1] else flat
+    return np.lib.stride_tricks.as_strided(
+        base, shape=(*batch_shape, *shape), strides=(*batch_strides, *(int(s) * item for s in strides)))
+
+
+def _injective(shape, strides) -> bool:
+    """No axis of extent > 1 with stride 0 (a validated record is then injective)."""
+    return all(n < 2 or s != 0 for n, s in zip(shape, strides))
+
+
 def _zero_plus(values: np.ndarray) -> np.ndarray:
     """0 + x, elementwise (turns -0 into +0)."""
     return np.zeros_like(values) + values
@@ -98,17 +116,24 @@ def accumulation(words, source: np.ndarray, coefficients=(), coefficient_records
     for index, (shape, sstr, so, dstr, do) in enumerate(records):
         if int(np.prod(shape)) == 0:
             continue
-        values = source[..., addresses(shape, sstr, so)]
+        fast = _injective(shape, dstr)
+        values = _view(source, so, shape, sstr) if fast else source[..., addresses(shape, sstr, so)]
         if index in factors:
             c, shared = _factor(factors[index], batch_shape)
             if shared and c == 0:
                 continue
             if not (shared and c == 1):
+                if fast and not shared:
+                    c = c.reshape(*batch_shape, *([1] * len(shape)))
                 values = _scale(c, values, source.dtype)
                 if not shared:
                     values = np.where(c == 0, np.zeros_like(values), values)
-        dst = addresses(shape, dstr, do)
-        _scatter_add(out, dst, values)
+        if fast:
+            # Records run in order; within one, destinations are distinct.
+            target = _view(out, do, shape, dstr)
+            target += values
+        else:
+            _scatter_add(out, addresses(shape, dstr, do), values)
     return out
 
 
@@ -141,20 +166,22 @@ def update(words, source: np.ndarray, base: np.ndarray, alpha, beta) -> np.ndarr
     batch_shape = base.shape[:-1]
     a, _ = _factor(alpha, batch_shape)
     b, _ = _factor(beta, batch_shape)
+    rank_a, rank_b = np.ndim(a), np.ndim(b)
     for shape, sstr, so, dstr, do in records:
         if int(np.prod(shape)) == 0:
             continue
-        dst = addresses(shape, dstr, do)
-        s = source[..., addresses(shape, sstr, so)]
-        o = base[..., dst]
+        s = _view(source, so, shape, sstr)
+        o = _view(base, do, shape, dstr)
+        ar = a.reshape(*a.shape, *([1] * (len(shape) - 1))) if rank_a else a
+        br = b.reshape(*b.shape, *([1] * (len(shape) - 1))) if rank_b else b
         a0, a1 = np.all(a == 0), np.all(a == 1)
         b0, b1 = np.all(b == 0), np.all(b == 1)
         if a0:
-            value = np.zeros_like(o) if b0 else (o if b1 else _scale(b, o, base.dtype))
+            value = np.zeros_like(o) if b0 else (o if b1 else _scale(br, o, base.dtype))
         else:
-            st = s if a1 else _scale(a, s, base.dtype)
-            value = st if b0 else (st + (o if b1 else _scale(b, o, base.dtype))).astype(base.dtype)
-        out[..., dst] = value
+            st = s if a1 else _scale(ar, s, base.dtype)
+            value = st if b0 else (st + (o if b1 else _scale(br, o, base.dtype))).astype(base.dtype)
+        _view(out, do, shape, dstr)[...] = value
     return out
 
 

@@ -16,6 +16,7 @@ LIBRARY_PATH = _build.LIBRARY
 S32, F32, F64, C64, C128 = 4, 11, 12, 15, 18
 OP_COPY, OP_UPDATE, OP_ACCUMULATION, OP_REDUCTION = 0, 1, 3, 4
 PLAN_OUTPUTS_DISJOINT = 1
+PLAN_WIDE_OFFSETS = 2
 
 c_i64p = ctypes.POINTER(ctypes.c_int64)
 
@@ -67,8 +68,8 @@ SIGNATURES = {
     "t0b_gemm_table_words": (ctypes.c_size_t, [ctypes.c_int64]),
     "t0b_gemm_table_build": (ctypes.c_int, [ctypes.c_int64, c_i64p, c_i64p, ctypes.c_char_p, ctypes.c_size_t]),
     "t0b_sector_gemm": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64, c_i64p, ctypes.c_void_p, ctypes.c_void_p,
-                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p,
-                                       ctypes.c_size_t]),
+                                       ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                       ctypes.c_int64, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
     "t0b_kernel_launches": (ctypes.c_uint64, []),
 }
 

@@ -92,6 +92,13 @@ void RequireAligned(const void* buffer, int element_bytes, const char* what) {
   }
 }
 
+// The device table holds 16-byte records read with vector loads.
+void RequireTableAligned(const int64_t* table) {
+  if (reinterpret_cast<uintptr_t>(table) % 16 != 0) {
+    throw t0b::InvalidArgument("device descriptor table is not 16-byte aligned");
+  }
+}
+
 const t0b::TableHeader& Header(const t0b_plan* plan) {
   return *reinterpret_cast<const t0b::TableHeader*>(plan->plan.table.data());
 }
@@ -179,6 +186,7 @@ void Sum(const t0b_plan* plan, int32_t operation, int32_t dtype, const void* sou
   Disjoint(source, src_bytes, output, out_bytes);
   const size_t table_bytes = p.table.size() * sizeof(int64_t);
   if (table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+  RequireTableAligned(table);
   Disjoint(table, table_bytes, output, out_bytes);
   uint64_t count = 1;
   int coef_bytes = 4;
@@ -186,6 +194,7 @@ void Sum(const t0b_plan* plan, int32_t operation, int32_t dtype, const void* sou
     coef_bytes = CoefficientBytes(coefficient_dtype, dtype);
     count = CoefficientCount(coefficient_count, batches);
     if (coefficients == nullptr) throw t0b::InvalidArgument("coefficient buffer is null");
+    RequireAligned(coefficients, coef_bytes, "coefficient");
     Disjoint(coefficients, Bytes(p.coefficient_rows * count, coef_bytes), output, out_bytes);
   } else {
     coefficient_dtype = T0B_S32;
@@ -281,6 +290,7 @@ int t0b_copy(const t0b_plan* plan, int32_t dtype, const void* source, void* outp
     if (b != 0 && p.output_size != 0 && output == nullptr) throw t0b::InvalidArgument("output buffer is null");
     if (b != 0 && p.source_size != 0 && source == nullptr) throw t0b::InvalidArgument("source buffer is null");
     if (device_table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+    RequireTableAligned(device_table);
     RequireAligned(source, p.element_bytes, "source");
     RequireAligned(output, p.element_bytes, "output");
     Disjoint(source, src_bytes, output, out_bytes);
@@ -329,12 +339,15 @@ int t0b_update(const t0b_plan* plan, int32_t dtype, const void* source, const vo
     }
     if (b != 0 && p.source_size != 0 && source == nullptr) throw t0b::InvalidArgument("source buffer is null");
     if (device_table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+    RequireTableAligned(device_table);
     RequireAligned(source, eb, "source");
     RequireAligned(base, eb, "base");
     RequireAligned(output, eb, "output");
     if (alpha == nullptr || beta == nullptr) throw t0b::InvalidArgument("update coefficient buffer is null");
     const int ab = CoefficientBytes(alpha_dtype, dtype);
     const int bb = CoefficientBytes(beta_dtype, dtype);
+    RequireAligned(alpha, ab, "alpha");
+    RequireAligned(beta, bb, "beta");
     const uint64_t a_count = CoefficientCount(alpha_count, batches);
     const uint64_t b_count = CoefficientCount(beta_count, batches);
     if (base != output) Disjoint(base, out_bytes, output, out_bytes);
@@ -387,11 +400,11 @@ int t0b_gemm_table_build(int64_t sectors, const int64_t* spec, int64_t* table, c
 }
 
 int t0b_sector_gemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const int64_t* device_table,
-                    const void* left, const void* right, void* output, void* stream, char* error,
-                    size_t error_size) {
+                    const void* left, int64_t left_size, const void* right, int64_t right_size, void* output,
+                    int64_t output_size, void* stream, char* error, size_t error_size) {
   return Guard(error, error_size, [&] {
-    t0b::SectorGemm(dtype, sectors, host_table, device_table, left, right, output,
-                    static_cast<cudaStream_t>(stream));
+    t0b::SectorGemm(dtype, sectors, host_table, device_table, left, left_size, right, right_size, output,
+                    output_size, static_cast<cudaStream_t>(stream));
   });
 }
 

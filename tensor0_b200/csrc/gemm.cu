@@ -13,6 +13,8 @@
 #include "engine.h"
 
 #include <algorithm>
+#include <string>
+#include <utility>
 #include <vector>
 
 namespace t0b {
@@ -292,22 +294,81 @@ void BuildGemmTable(int64_t sectors, const int64_t* spec, int64_t* table) {
   }
 }
 
+// Bytes of one element of a GEMM operand, or 0 for an unsupported dtype.
+int GemmElementBytes(int32_t dtype) {
+  switch (dtype) {
+    case 11: return 4;
+    case 12: case 15: return 8;
+    case 18: return 16;
+    default: return 0;
+  }
+}
+
 void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const int64_t* device_table,
-                const void* left, const void* right, void* output, cudaStream_t stream) {
+                const void* left, int64_t left_size, const void* right, int64_t right_size, void* output,
+                int64_t output_size, cudaStream_t stream) {
+  const int eb = GemmElementBytes(dtype);
+  if (eb == 0) throw InvalidArgument("sector GEMM supports only F32/F64/C64/C128");
   if (sectors < 0) throw InvalidArgument("sector count must be nonnegative");
+  if (left_size < 0 || right_size < 0 || output_size < 0) throw InvalidArgument("GEMM operand sizes must be nonnegative");
   if (sectors == 0) return;
   if (host_table == nullptr || device_table == nullptr) throw InvalidArgument("GEMM table is null");
+  // Every row must address inside the operands, and output blocks must not
+  // overlap one another: all checks run before the launch.
+  auto span = [](int64_t offset, int64_t rows, int64_t cols, int64_t size, const char* what) {
+    uint64_t count = 0, end = 0;
+    if (!CheckedMul(static_cast<uint64_t>(rows), static_cast<uint64_t>(cols), &count) ||
+        !CheckedAdd(static_cast<uint64_t>(offset), count, &end) || (count != 0 && end > static_cast<uint64_t>(size))) {
+      throw InvalidArgument(std::string("GEMM ") + what + " block lies outside its operand");
+    }
+    return count;
+  };
   int64_t tiles = 0;
+  std::vector<std::pair<int64_t, int64_t>> blocks;
+  blocks.reserve(static_cast<std::size_t>(sectors));
   for (int64_t s = 0; s < sectors; ++s) {
     const int64_t* row = host_table + s * kGemmRow;
     for (int i = 0; i < 6; ++i) {
       if (row[i] < 0) throw InvalidArgument("GEMM sizes and offsets must be nonnegative");
     }
+    if (row[0] > (int64_t{1} << 31) || row[1] > (int64_t{1} << 31) || row[2] > (int64_t{1} << 40)) {
+      throw InvalidArgument("GEMM block extents are too large");
+    }
     if (row[6] != tiles) throw InvalidArgument("GEMM table tile prefix is inconsistent; build it with t0b_gemm_table_build");
+    const uint64_t c_count = span(row[5], row[0], row[1], output_size, "output");
+    if (row[2] != 0) {
+      span(row[3], row[0], row[2], left_size, "left");
+      span(row[4], row[2], row[1], right_size, "right");
+    }
+    if (c_count != 0) blocks.emplace_back(row[5], row[5] + static_cast<int64_t>(c_count));
     tiles += ((row[0] + kTile - 1) / kTile) * ((row[1] + kTile - 1) / kTile);
+  }
+  std::sort(blocks.begin(), blocks.end());
+  for (std::size_t i = 1; i < blocks.size(); ++i) {
+    if (blocks[i].first < blocks[i - 1].second) throw InvalidArgument("GEMM output blocks overlap");
   }
   if (tiles == 0) return;
   if (left == nullptr || right == nullptr || output == nullptr) throw InvalidArgument("GEMM operand is null");
+  // Operands are staged with element-sized asynchronous copies (16 bytes for C128).
+  for (const void* buffer : {static_cast<const void*>(left), static_cast<const void*>(right),
+                             static_cast<const void*>(output)}) {
+    if (reinterpret_cast<uintptr_t>(buffer) % static_cast<uintptr_t>(eb) != 0) {
+      throw InvalidArgument("GEMM operand buffer is not aligned to its element size");
+    }
+  }
+  auto overlap = [](const void* a, uint64_t a_bytes, const void* b, uint64_t b_bytes) {
+    if (a_bytes == 0 || b_bytes == 0) return false;
+    const auto x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x <= y ? y - x < a_bytes : x - y < b_bytes;
+  };
+  const uint64_t out_bytes = static_cast<uint64_t>(output_size) * eb;
+  if (overlap(left, static_cast<uint64_t>(left_size) * eb, output, out_bytes) ||
+      overlap(right, static_cast<uint64_t>(right_size) * eb, output, out_bytes)) {
+    throw InvalidArgument("input and output buffers overlap");
+  }
+  if (overlap(device_table, static_cast<uint64_t>(sectors) * kGemmRow * sizeof(int64_t), output, out_bytes)) {
+    throw InvalidArgument("device descriptor table overlaps the output");
+  }
   const int64_t grid = std::min<int64_t>(tiles, int64_t{SmCountGemm()} * 4);
   switch (dtype) {
     case 12:

@@ -11,7 +11,10 @@ namespace t0b {
 constexpr int kGemmRow = 8;
 
 void BuildGemmTable(int64_t sectors, const int64_t* spec, int64_t* table);
+// Validates every table row against the operand sizes (elements), the
+// operands' alignment and overlaps, then launches; throws InvalidArgument.
 void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const int64_t* device_table,
-                const void* left, const void* right, void* output, cudaStream_t stream);
+                const void* left, int64_t left_size, const void* right, int64_t right_size, void* output,
+                int64_t output_size, cudaStream_t stream);
 
 }  // namespace t0b

@@ -15,7 +15,7 @@ namespace t0b {
 namespace {
 
 constexpr uint64_t kExtentLimit = uint64_t{1} << 30;   // per-axis extent kept in int32
-constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest exact overlap check
+constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest address span checked with a bitmap
 
 // Bytes of shared memory one map tile may stage (before row padding): 16 KB
 // for copy and accumulation (eight 128-thread CTAs per SM), 32 KB for update,
@@ -107,24 +107,132 @@ void ForEachOwnerAddress(const Record& record, Visit visit) {
   }
 }
 
-// Exact pairwise-disjointness proof over the owner addresses, for sizes where
-// a bit per output element is affordable.
-bool ProveDisjoint(const std::vector<const Record*>& records, uint64_t output_size) {
+// Address interval [lo, hi] a record's owner (map) axes reach.
+void OwnerInterval(const Record& record, int64_t* lo, int64_t* hi) {
+  *lo = *hi = record.dst_off;
+  for (std::size_t a = 0; a < record.shape.size(); ++a) {
+    if (record.fiber[a] || record.shape[a] < 2) continue;
+    const int64_t span = static_cast<int64_t>(record.shape[a] - 1) * record.dstr[a];
+    if (span > 0) *hi += span; else *lo += span;
+  }
+}
+
+// A record's owner addresses written as origin + q * radix + m with m in
+// [0, radix): axes whose stride is a multiple of the radix move q, the others
+// move m.  Valid when the m span stays inside [0, radix), so q and m are
+// unique; the record then lies inside the rectangle [q_lo, q_hi] x [m_lo, m_hi].
+struct Rectangle {
+  int64_t q_lo, q_hi, m_lo, m_hi;
+};
+
+bool Decompose(const Record& record, int64_t origin, int64_t radix, Rectangle* out) {
+  const int64_t at = record.dst_off - origin;
+  Rectangle r{at / radix, at / radix, at % radix, at % radix};
+  for (std::size_t a = 0; a < record.shape.size(); ++a) {
+    if (record.fiber[a] || record.shape[a] < 2) continue;
+    const int64_t n = static_cast<int64_t>(record.shape[a] - 1), s = record.dstr[a];
+    if (s % radix == 0) {
+      (s > 0 ? r.q_hi : r.q_lo) += n * (s / radix);
+    } else {
+      (s > 0 ? r.m_hi : r.m_lo) += n * s;
+    }
+  }
+  if (r.m_lo < 0 || r.m_hi >= radix) return false;
+  *out = r;
+  return true;
+}
+
+// Pairwise-disjoint rectangles, by a sweep over q; false when inconclusive
+// (an overlap, or more comparisons than the budget allows).
+bool RectanglesDisjoint(std::vector<Rectangle>& rects) {
+  std::sort(rects.begin(), rects.end(), [](const Rectangle& a, const Rectangle& b) { return a.q_lo < b.q_lo; });
+  std::vector<const Rectangle*> active;
+  uint64_t budget = uint64_t{1} << 26;
+  for (const Rectangle& r : rects) {
+    std::size_t keep = 0;
+    for (const Rectangle* other : active) {
+      if (other->q_hi < r.q_lo) continue;
+      if (budget-- == 0) return false;
+      if (!(other->m_hi < r.m_lo || r.m_hi < other->m_lo)) return false;
+      active[keep++] = other;
+    }
+    active.resize(keep);
+    active.push_back(&r);
+  }
+  return true;
+}
+
+// Exact check by a bit per address over [lo, hi].
+bool BitmapDisjoint(const std::vector<const Record*>& records, int64_t lo, int64_t hi) {
+  const uint64_t span = static_cast<uint64_t>(hi - lo) + 1;
   uint64_t total = 0;
   for (const Record* record : records) total += OwnerCount(*record);
-  if (total > output_size) return false;
-  if (output_size > kProofLimit || total > kProofLimit) return false;
-  std::vector<uint64_t> bits((output_size + 63) / 64, 0);
+  if (total > span || span > kProofLimit) return false;
+  std::vector<uint64_t> bits((span + 63) / 64, 0);
   bool disjoint = true;
   for (const Record* record : records) {
     ForEachOwnerAddress(*record, [&](int64_t address) {
-      uint64_t& word = bits[static_cast<uint64_t>(address) >> 6];
-      const uint64_t mask = uint64_t{1} << (address & 63);
+      const uint64_t at = static_cast<uint64_t>(address - lo);
+      uint64_t& word = bits[at >> 6];
+      const uint64_t mask = uint64_t{1} << (at & 63);
       if (word & mask) { disjoint = false; return false; }
       word |= mask;
       return true;
     });
     if (!disjoint) return false;
+  }
+  return true;
+}
+
+// Pairwise disjointness of the records' owner addresses (each record's own
+// injectivity is validated when the layout is decoded).  Records whose
+// address intervals do not meet are disjoint; each cluster of meeting
+// intervals is proven either by a radix decomposition (a packed block's
+// sub-blocks are rectangles of rows x columns under the block's row stride)
+// or, over spans up to 2^28 addresses, exactly with a bitmap.
+bool ProveDisjoint(const std::vector<const Record*>& records, uint64_t output_size) {
+  uint64_t total = 0;
+  for (const Record* record : records) total += OwnerCount(*record);
+  if (total > output_size) return false;
+  struct Item { int64_t lo, hi; const Record* record; };
+  std::vector<Item> items;
+  items.reserve(records.size());
+  for (const Record* record : records) {
+    Item item{0, 0, record};
+    OwnerInterval(*record, &item.lo, &item.hi);
+    items.push_back(item);
+  }
+  std::sort(items.begin(), items.end(), [](const Item& a, const Item& b) { return a.lo < b.lo; });
+  std::size_t begin = 0;
+  while (begin < items.size()) {
+    std::size_t end = begin + 1;
+    int64_t reach = items[begin].hi;
+    while (end < items.size() && items[end].lo <= reach) reach = std::max(reach, items[end++].hi);
+    if (end - begin > 1) {
+      std::vector<const Record*> cluster;
+      std::map<int64_t, int> radices;
+      for (std::size_t i = begin; i < end; ++i) {
+        cluster.push_back(items[i].record);
+        const Record& r = *items[i].record;
+        for (std::size_t a = 0; a < r.shape.size(); ++a) {
+          if (!r.fiber[a] && r.shape[a] > 1 && AbsStride(r.dstr[a]) > 1) ++radices[static_cast<int64_t>(AbsStride(r.dstr[a]))];
+        }
+      }
+      std::vector<std::pair<int, int64_t>> candidates;
+      for (const auto& [radix, count] : radices) candidates.emplace_back(-count, radix);
+      std::sort(candidates.begin(), candidates.end());
+      bool proven = false;
+      for (std::size_t c = 0; c < candidates.size() && c < 8 && !proven; ++c) {
+        std::vector<Rectangle> rects(cluster.size());
+        bool all = true;
+        for (std::size_t i = 0; i < cluster.size() && all; ++i) {
+          all = Decompose(*cluster[i], items[begin].lo, candidates[c].second, &rects[i]);
+        }
+        proven = all && RectanglesDisjoint(rects);
+      }
+      if (!proven && !BitmapDisjoint(cluster, items[begin].lo, reach)) return false;
+    }
+    begin = end;
   }
   return true;
 }
@@ -467,6 +575,7 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     }
   }
 
+  if ((flags & 2u) != 0) plan.map_wide = true;
   plan.has_map = !map_records.empty();
   plan.has_reduce = !groups.empty();
   plan.map_tiles = static_cast<uint64_t>(tiles);

@@ -13,6 +13,7 @@
 // loads this library holds it until the process exits.
 #include "../../include/tensor0_b200.h"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -27,8 +28,33 @@ constexpr int kMaxDevices = 64;
 // address must come from cudaGetSymbolAddress on each device.
 __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-void* g_scratch_address[kMaxDevices] = {};
+// The array's device address per device, with the context it was looked up
+// in.  A module is loaded per context, so a different current context (a
+// driver-API context, or a primary context recreated after cudaDeviceReset
+// under a new handle) gets its own lookup.
+struct ScratchAddress {
+  CUcontext context = nullptr;
+  void* address = nullptr;
+};
+ScratchAddress g_scratch_address[kMaxDevices];
 std::mutex g_setup;
+
+// cuCtxGetCurrent through the runtime's driver entry point, so the library
+// needs no link against the driver library.
+CUresult CurrentContext(CUcontext* context) {
+  using Function = CUresult (*)(CUcontext*);
+  static Function function = [] {
+    void* pointer = nullptr;
+    cudaDriverEntryPointQueryResult found{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &pointer, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess) {
+      return static_cast<Function>(nullptr);
+    }
+    return reinterpret_cast<Function>(pointer);
+  }();
+  if (function == nullptr) return CUDA_ERROR_NOT_FOUND;
+  return function(context);
+}
 
 int Fail(char* error, size_t size, int status, const char* text) {
   if (error != nullptr && size != 0) std::snprintf(error, size, "tensor0-b200: %s", text);
@@ -71,9 +97,17 @@ extern "C" int t0b_reduction_static_scratch(const t0b_plan* plan, int32_t dtype,
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
       return Fail(error, error_size, 2, "cannot identify the current CUDA device");
     }
+    // No context is current yet on a thread where the runtime has not touched
+    // the device; the symbol lookup below then initialises the primary one.
+    CUcontext context = nullptr;
+    if (CurrentContext(&context) != CUDA_SUCCESS) {
+      return Fail(error, error_size, 2, "cannot identify the current CUDA context");
+    }
     std::lock_guard<std::mutex> lock(g_setup);
-    if (g_scratch_address[device] == nullptr) {
-      // Once per device, with that device current: resolve the array's device address.
+    ScratchAddress& cached = g_scratch_address[device];
+    if (cached.address == nullptr || context == nullptr || cached.context != context) {
+      // Once per device (and context), with that device current: resolve the
+      // array's device address.
       void* address = nullptr;
       const cudaError_t status = cudaGetSymbolAddress(&address, g_static_scratch);
       if (status != cudaSuccess || address == nullptr) {
@@ -82,9 +116,13 @@ extern "C" int t0b_reduction_static_scratch(const t0b_plan* plan, int32_t dtype,
                       cudaGetErrorString(status));
         return Fail(error, error_size, 2, text);
       }
-      g_scratch_address[device] = address;
+      if (context == nullptr && (CurrentContext(&context) != CUDA_SUCCESS || context == nullptr)) {
+        return Fail(error, error_size, 2, "cannot identify the current CUDA context");
+      }
+      cached.context = context;
+      cached.address = address;
     }
-    scratch = g_scratch_address[device];
+    scratch = cached.address;
   }
   return t0b_reduction(plan, dtype, source, output, batches, coefficients, coefficient_dtype, coefficient_count,
                        scratch, device_table, stream, error, error_size);

@@ -124,7 +124,7 @@ class Plan:
     """Prepared state of one operation over one layout (the reference's instantiate)."""
 
     def __init__(self, operation: int, words: np.ndarray, *, element_bytes: int,
-                 coefficient_records=(), outputs_disjoint: bool = False):
+                 coefficient_records=(), outputs_disjoint: bool = False, wide_offsets: bool = False):
         self._lib = _native.lib()
         words = np.ascontiguousarray(words, dtype=np.int64)
         records = np.ascontiguousarray(np.asarray(coefficient_records, dtype=np.int64))
@@ -133,7 +133,8 @@ class Plan:
         status = self._lib.t0b_plan_create(
             operation, words.ctypes.data_as(_native.c_i64p), words.size,
             records.ctypes.data_as(_native.c_i64p) if records.size else None, records.size,
-            element_bytes, _native.PLAN_OUTPUTS_DISJOINT if outputs_disjoint else 0,
+            element_bytes, (_native.PLAN_OUTPUTS_DISJOINT if outputs_disjoint else 0)
+            | (_native.PLAN_WIDE_OFFSETS if wide_offsets else 0),
             ctypes.byref(handle), err, len(err))
         _native.check(status, err)
         self._handle = handle
@@ -346,8 +347,8 @@ def sector_gemm(plan: GemmPlan, left: torch.Tensor, right: torch.Tensor, out: to
     err = _native.error_buffer()
     status = _native.lib().t0b_sector_gemm(
         _storage_code(out), plan.sectors, plan.table.ctypes.data_as(_native.c_i64p),
-        plan.device_table(out.device).data_ptr(), left.data_ptr(), right.data_ptr(), out.data_ptr(),
-        _stream(out.device), err, len(err))
+        plan.device_table(out.device).data_ptr(), left.data_ptr(), left.numel(), right.data_ptr(), right.numel(),
+        out.data_ptr(), out.numel(), _stream(out.device), err, len(err))
     _native.check(status, err)
     return out
 

@@ -158,3 +158,64 @@ def test_map_tiling_covers_every_element(lib):
     assert engine.info["full_coverage"] == 1
     assert engine.info["kernels_per_call"] == 1
     assert engine.info["records"] == 85
+
+
+def gemm_call(lib, dtype, spec, left, left_size, right, right_size, output, output_size):
+    plan = stride.GemmPlan(np.asarray(spec))
+    err = _native.error_buffer()
+    status = lib.t0b_sector_gemm(dtype, plan.sectors, plan.table.ctypes.data_as(_native.c_i64p),
+                                 ctypes.c_void_p(0x90000), ctypes.c_void_p(left), left_size, ctypes.c_void_p(right),
+                                 right_size, ctypes.c_void_p(output), output_size, None, err, len(err))
+    return status, err.value
+
+
+def test_sector_gemm_validates_operands_before_any_launch(lib):
+    """Rows outside their operands, overlapping output blocks, misaligned or
+    overlapping operands are rejected with status 1 and launch nothing."""
+    launches = lib.t0b_kernel_launches()
+    spec = [[4, 4, 4, 0, 0, 0]]
+    status, message = gemm_call(lib, _native.F64, spec, 0x1000, 15, 0x2000, 16, 0x3000, 16)
+    assert status == 1 and b"left block lies outside" in message
+    status, message = gemm_call(lib, _native.F64, spec, 0x1000, 16, 0x2000, 12, 0x3000, 16)
+    assert status == 1 and b"right block lies outside" in message
+    status, message = gemm_call(lib, _native.F64, spec, 0x1000, 16, 0x2000, 16, 0x3000, 15)
+    assert status == 1 and b"output block lies outside" in message
+    status, message = gemm_call(lib, _native.F64, [[2, 2, 2, 0, 0, 0], [2, 2, 2, 0, 0, 3]],
+                                0x1000, 4, 0x2000, 4, 0x3000, 8)
+    assert status == 1 and b"output blocks overlap" in message
+    status, message = gemm_call(lib, _native.C128, spec, 0x1000, 16, 0x2008, 16, 0x3000, 16)
+    assert status == 1 and b"not aligned" in message
+    status, message = gemm_call(lib, _native.F32, spec, 0x1000, 16, 0x2000, 16, 0x1020, 16)
+    assert status == 1 and b"overlap" in message
+    assert lib.t0b_kernel_launches() == launches
+
+
+def test_disjointness_is_proven_for_large_packed_permutes(lib):
+    """Without the producer's assertion the planner proves the full-size U(1)
+    4-leg permute disjoint (1.02e9 outputs, beyond a bitmap's reach) by the
+    block-row radix decomposition, so accumulation stays one map launch."""
+    from tensor0_b200.structure import U1Irrep, hom, space
+    from tensor0_b200.tensor_map import permute_plan
+    degs = {q: int(round(64 * np.exp(-q * q / 8))) for q in range(-4, 5)}
+    v = space(U1Irrep, degs)
+    for p in (((2, 0), (3, 1)), ((1, 0), (3, 2)), ((3,), (0, 1, 2))):
+        plan = permute_plan(hom((v, v), (v, v)), *p)
+        engine = stride.Plan(_native.OP_ACCUMULATION, plan.words, element_bytes=4,
+                             coefficient_records=np.arange(len(plan.transform.src)))
+        assert engine.output_size > 1 << 28
+        assert engine.info["kernels_per_call"] == 1 and engine.info["full_coverage"] == 1
+
+
+def test_overlap_beyond_the_bitmap_reach_is_not_proven(lib):
+    """Records that share an address over a span too large for the exact
+    check run in record order (one reduce wave per record)."""
+    big = 1 << 29
+    records = [stride.AffineRecord((2,), (1,), 0, (big,), 0), stride.AffineRecord((2,), (1,), 2, (big,), big)]
+    words = stride.encode_layout(records, source_size=4, output_size=2 * big + 1)
+    engine = stride.Plan(_native.OP_ACCUMULATION, words, element_bytes=8, coefficient_records=[0, 1])
+    assert engine.info["kernels_per_call"] == 4
+    interleaved = [stride.AffineRecord((3, 2), (2, 1), 0, (big, 1), 0),
+                   stride.AffineRecord((3, 2), (2, 1), 6, (big, 1), 2)]
+    words = stride.encode_layout(interleaved, source_size=12, output_size=2 * big + 4)
+    engine = stride.Plan(_native.OP_ACCUMULATION, words, element_bytes=8, coefficient_records=[0, 1])
+    assert engine.info["kernels_per_call"] == 1

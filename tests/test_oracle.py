@@ -121,3 +121,62 @@ def test_sector_gemm_oracle_is_blockwise_matmul():
     np.testing.assert_allclose(out[:12].reshape(3, 4), left[:15].reshape(3, 5) @ right[:20].reshape(5, 4))
     assert np.all(out[12:16] == 0)
     np.testing.assert_allclose(out[16:19], (left[15:17].reshape(1, 2) @ right[20:26].reshape(2, 3)).reshape(-1))
+
+
+def random_reduction_layout(rng, source_size, records):
+    """Random reduction records: a permuted strided box of the source per
+    record, some axes summed; outputs either a fresh contiguous region or the
+    region of an earlier record with the same open shape (contributions add)."""
+    out, shapes, roles, regions, cursor = [], [], [], [], 0
+    for _ in range(records):
+        rank = int(rng.integers(1, 5))
+        shape = tuple(int(n) for n in rng.integers(1, 5, size=rank))
+        role = tuple(bool(r) for r in rng.integers(0, 2, size=rank))
+        count = int(np.prod(shape))
+        if count > source_size:
+            continue
+        perm = rng.permutation(rank)
+        src_contig = stride.contiguous_strides(tuple(shape[p] for p in perm))
+        sstr = [0] * rank
+        for i, p in enumerate(perm):
+            sstr[p] = src_contig[i]
+        sign = rng.choice([-1, 1], size=rank)
+        sstr = [int(s * g) for s, g in zip(sstr, sign)]
+        soff = int(rng.integers(0, source_size - count + 1))
+        soff += sum((n - 1) * (-s) for n, s in zip(shape, sstr) if s < 0)
+        if soff + sum((n - 1) * s for n, s in zip(shape, sstr) if s > 0) >= source_size:
+            continue
+        open_shape = tuple(n for n, r in zip(shape, role) if not r)
+        reuse = [d for s, d in regions if s == open_shape]
+        if reuse and rng.random() < 0.5:
+            dst_off = int(rng.choice(reuse))
+        else:
+            dst_off = cursor
+            regions.append((open_shape, cursor))
+            cursor += int(np.prod(open_shape)) + int(rng.integers(0, 2))
+        open_strides = iter(stride.contiguous_strides(open_shape))
+        dstr = tuple(1 if r else next(open_strides) for r in role)
+        out.append(stride.AffineRecord(shape, tuple(sstr), soff, dstr, dst_off))
+        shapes.append(tuple(1 if r else n for n, r in zip(shape, role)))
+        roles.append(role)
+    return out, shapes, roles, max(cursor, 1)
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.complex64, np.complex128])
+def test_random_reductions_match_compiled_reference(seed, dtype):
+    rng = np.random.default_rng(200 + seed)
+    records, shapes, roles, output_size = random_reduction_layout(rng, 300, 14)
+    words = stride.encode_reduction_layout(records, output_shapes=shapes, reduction_axes=roles,
+                                           source_size=300, output_size=output_size)
+    complex_storage = np.iscomplexobj(np.zeros(1, dtype))
+    x = rng.standard_normal((2, 300)) + (1j * rng.standard_normal((2, 300)) if complex_storage else 0)
+    x = x.astype(dtype)
+    real = np.float32 if dtype in (np.float32, np.complex64) else np.float64
+    coefficients = [real(c) for c in rng.choice([0.0, 1.0, -0.5, 2.0], size=len(records))]
+    mine = so.reduction(words, x, coefficients, np.arange(len(records)))
+    theirs = ref.reduction(words, x, output_size, coefficients, np.arange(len(records)))
+    tolerance = 1e-6 if real == np.float32 else 1e-12
+    scale = max(float(np.max(np.abs(theirs))), 1.0)
+    assert float(np.max(np.abs(mine - theirs))) <= tolerance * scale
