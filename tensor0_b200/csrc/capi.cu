@@ -241,10 +241,10 @@ int t0b_plan_create(int32_t operation, const int64_t* words, size_t word_count,
     const auto& h = *reinterpret_cast<const t0b::TableHeader*>(built->plan.table.data());
     int64_t tile = 0, box = 0;
     t0b::MapTileElements(reinterpret_cast<const t0b::MapRecord*>(built->plan.table.data() + h.map_offset),
-                         h.map_records, &tile, &box);
+                         h.map_records, element_bytes, &tile, &box);
     // Update plans also stage the destination's base values, in the tile's layout.
     built->tile_elems = tile;
-    built->map_smem = static_cast<int>((operation == T0B_OP_UPDATE ? 2 * tile : tile) * element_bytes);
+    built->map_smem = static_cast<int>(t0b::MapSharedBytes(operation, tile, element_bytes));
     *plan = built.release();
     g_created.fetch_add(1, std::memory_order_relaxed);
   });

@@ -71,21 +71,30 @@ struct Runs {
 // the plan marked a record wide).  Shared memory holds the tile in
 // destination order: element (x, y, z) at x + px * y + pz * z, px = ex | 1
 // (odd, so source runs, which step px, hit distinct banks) and pz = px * ey.
+// A rectangular tile (MapMode kRect): box ex x ey x ez, source element
+// (x, y, z) at x * sx + y + z * sz, destination at x + y * dy + z * dz.
+template <typename Off>
+struct RectBox {
+  int ex, ey, ez, px, pz;
+  Off sx, sz, dy, dz;
+};
+
 template <typename Off>
 struct TileState {
   int64_t so, dof;        // element offsets of the tile origin, batch included
   Runs<Off> load;         // source runs into shared memory
   Runs<Off> store;        // destination runs out of shared memory (also the update's base loads)
+  RectBox<Off> box;       // rectangular tiles: the fixed thread map's box (runs unused)
   int64_t batch;
   int slot;
+  int rect;
   alignas(16) unsigned char coef[32];   // the tile's coefficients, fetched by the decoding thread
 };
 
-// Thread 0 only: decode tile `local` of record `rec` in `batch`.
+// Thread 0 only: decode tile `local` of record `r` in `batch`.
 template <typename Off, int kThreadsPerCta>
-__device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_t batch, int64_t local,
+__device__ __forceinline__ void DecodeTile(const MapArgs& a, const MapRecord& r, int64_t batch, int64_t local,
                                            TileState<Off>& s) {
-  const MapRecord& r = a.recs[rec];
   uint32_t q = static_cast<uint32_t>(local - r.tile_begin);
   uint32_t chunk[3];
 #pragma unroll
@@ -115,6 +124,13 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   const Off sx = static_cast<Off>(r.s[0]), sy = static_cast<Off>(r.s[1]), sz = static_cast<Off>(r.s[2]);
   const Off dx = static_cast<Off>(r.d[0]), dy = static_cast<Off>(r.d[1]), dz = static_cast<Off>(r.d[2]);
   const int px = ex | 1, pz = px * ey;
+  s.batch = batch;
+  s.slot = r.coef_slot;
+  s.rect = r.mode == kRect;
+  if (s.rect) {
+    s.box = RectBox<Off>{ex, ey, ez, px, pz, sx, sz, dy, dz};
+    return;
+  }
   const FastDiv by_x = Division(r.div_extent[last_x ? 1 : 0]);
   const FastDiv by_y = Division(r.div_extent[last_y ? 3 : 2]);
   // Destination: when (x, y) is contiguous on both sides (an odd ex needs no
@@ -136,8 +152,6 @@ __device__ __forceinline__ void DecodeTile(const MapArgs& a, int64_t rec, int64_
   } else {
     l = Runs<Off>{sx, sz, sy, 1, pz, px, ex, ez, ey, by_x, by_y};
   }
-  s.batch = batch;
-  s.slot = r.coef_slot;
 }
 
 // Per-operation element rule applied when a value reaches the destination.
@@ -348,8 +362,8 @@ __device__ __forceinline__ T LoadShared(uint32_t addr) {
 }
 
 // Asynchronous global -> shared copy of one element (no register round trip).
-// The copies are ordered against shared-memory reads by WaitAsync and the
-// CTA barrier that follows it.
+// The copies are ordered against shared-memory reads by the wait on their
+// cp.async group and the CTA barrier that follows it.
 template <int Bytes>
 __device__ __forceinline__ void CopyAsync(uint32_t smem, const void* gmem) {
   if constexpr (Bytes == 16) {
@@ -359,7 +373,70 @@ __device__ __forceinline__ void CopyAsync(uint32_t smem, const void* gmem) {
   }
 }
 
-__device__ __forceinline__ void WaitAsync() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Rectangular tiles.  Every element of the box goes through shared memory at
+// x + px * y + pz * z.  Loads: lane l takes y = l and l + 32 (consecutive
+// source addresses, and shared-memory words px apart: distinct banks as px is
+// odd), warps take rows x.  Stores: lane l takes x = l and l + 32, warps take
+// rows y.  Both halves of a row are issued back to back, and each thread walks
+// its rows with constant pointer steps.
+template <int kCta, typename T, typename Off, typename Move>
+__device__ __forceinline__ void RectRows(int lanes_extent, int rows_extent, int ez, Off row_step, Off z_step,
+                                         int s_lane, int s_row, int s_z, T* base, uint32_t sbase, Move&& move) {
+  constexpr int kW = kCta / 32;
+  constexpr uint32_t B = sizeof(T);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane >= lanes_extent) return;
+  const bool second = lane + 32 < lanes_extent;
+  const Off row_w = row_step * kW;
+  const uint32_t srow_w = static_cast<uint32_t>(s_row * kW) * B;
+  const uint32_t s_half = static_cast<uint32_t>(32 * s_lane) * B;
+  for (int z = 0; z < ez; ++z) {
+    T* g = base + (z * z_step + warp * row_step + lane);
+    uint32_t sm = sbase + static_cast<uint32_t>(s_z * z + s_row * warp + s_lane * lane) * B;
+    int row = warp;
+    if (lanes_extent > 32) {
+      for (; row + kW < rows_extent; row += 2 * kW) {
+        move(g, sm);
+        if (second) move(g + 32, sm + s_half);
+        move(g + row_w, sm + srow_w);
+        if (second) move(g + row_w + 32, sm + srow_w + s_half);
+        g += 2 * row_w;
+        sm += 2 * srow_w;
+      }
+      if (row < rows_extent) {
+        move(g, sm);
+        if (second) move(g + 32, sm + s_half);
+      }
+    } else {
+      for (; row + 3 * kW < rows_extent; row += 4 * kW) {
+        move(g, sm);
+        move(g + row_w, sm + srow_w);
+        move(g + 2 * row_w, sm + 2 * srow_w);
+        move(g + 3 * row_w, sm + 3 * srow_w);
+        g += 4 * row_w;
+        sm += 4 * srow_w;
+      }
+      for (; row < rows_extent; row += kW) {
+        move(g, sm);
+        g += row_w;
+        sm += srow_w;
+      }
+    }
+  }
+}
+
+// Source rows (lanes along Y, rows along X) into the tile.
+template <int kCta, typename T, typename Off, typename Move>
+__device__ __forceinline__ void RectSourceRows(const RectBox<Off>& b, T* src, uint32_t tile_s, Move&& move) {
+  RectRows<kCta, T, Off>(b.ey, b.ex, b.ez, b.sx, b.sz, b.px, 1, b.pz, src, tile_s, move);
+}
+
+// Destination rows (lanes along X, rows along Y) of the tile.
+template <int kCta, typename T, typename Off, typename Move>
+__device__ __forceinline__ void RectDestinationRows(const RectBox<Off>& b, T* dst, uint32_t tile_s, Move&& move) {
+  RectRows<kCta, T, Off>(b.ex, b.ey, b.ez, b.dy, b.dz, 1, b.px, b.pz, dst, tile_s, move);
+}
 
 // Issue the asynchronous loads of one tile: the source runs into the tile
 // and, for update, the destination's base values into the same positions of
@@ -369,6 +446,18 @@ __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Of
                                          uint32_t base_s) {
   const E emit(st.coef);
   auto copy = [](const T* p, uint32_t s) { CopyAsync<sizeof(T)>(s, p); };
+  if (st.rect) {
+    const RectBox<Off> box = st.box;
+    if (!emit.SkipSource()) {
+      RectSourceRows<kThreadsPerCta>(box, static_cast<const T*>(args.src) + st.so, tile_s, copy);
+    }
+    if constexpr (E::kReadsBase) {
+      if (emit.NeedsBase()) {
+        RectDestinationRows<kThreadsPerCta>(box, static_cast<const T*>(args.base) + st.dof, base_s, copy);
+      }
+    }
+    return;
+  }
   if (!emit.SkipSource()) {
     Walk<Off, kThreadsPerCta, false>(st.load, static_cast<const T*>(args.src) + st.so, tile_s, copy);
   }
@@ -377,36 +466,95 @@ __device__ __forceinline__ void LoadTile(const MapArgs& args, const TileState<Of
   }
 }
 
-// Thread 0 only: advance the tile cursor (record, batch, tile within the
-// batch) to the next tile and decode it.
-template <typename E, typename Off, int kThreadsPerCta>
-__device__ __forceinline__ void DecodeNext(const MapArgs& args, int64_t* cursor, TileState<Off>& next) {
-  int64_t rec = cursor[0], batch = cursor[1], local = cursor[2] + 1;
-  if (local == args.tiles_per_batch) { local = 0; ++batch; rec = 0; }
-  while (rec + 1 < args.nrec && args.recs[rec + 1].tile_begin <= local) ++rec;
-  cursor[0] = rec; cursor[1] = batch; cursor[2] = local;
-  DecodeTile<Off, kThreadsPerCta>(args, rec, batch, local, next);
-  E::Fetch(args, next.slot, next.batch, next.coef);
+// The decoding thread's position: the current record, copied into shared
+// memory once per record (a CTA walks a contiguous tile range, so records
+// change rarely), the next record's first tile, and the coefficients of the
+// current (record, batch).  Decoding a tile then reads no global memory.
+struct alignas(16) MapCursor {
+  MapRecord rec;
+  int64_t rec_index;
+  int64_t next_begin;     // first tile of record rec_index + 1 (or past the end)
+  int64_t batch;
+  int64_t local;          // tile within the batch
+  int64_t coef_batch;     // batch the staged coefficients belong to (-1: none)
+  int64_t pad_;
+  alignas(16) unsigned char coef[32];
+};
+
+__device__ __forceinline__ void LoadRecord(const MapArgs& args, int64_t index, MapCursor& c) {
+  static_assert(sizeof(MapRecord) % 16 == 0, "records are copied in 16-byte words");
+  const int4* from = reinterpret_cast<const int4*>(args.recs + index);
+  int4* to = reinterpret_cast<int4*>(&c.rec);
+#pragma unroll
+  for (int k = 0; k < static_cast<int>(sizeof(MapRecord) / 16); ++k) to[k] = from[k];
+  c.rec_index = index;
+  c.next_begin = index + 1 < args.nrec ? args.recs[index + 1].tile_begin : (int64_t{1} << 62);
+  c.coef_batch = -1;
 }
 
-// One persistent CTA walks a contiguous range of tiles.  Per tile: issue the
-// asynchronous loads, let thread 0 decode the next tile while they fly, wait,
-// then write the destination runs out of shared memory.
+// Thread 0 only: decode the cursor's tile into `next`, staging its coefficients.
+template <typename E, typename Off, int kThreadsPerCta>
+__device__ __forceinline__ void DecodeAt(const MapArgs& args, MapCursor& c, TileState<Off>& next) {
+  DecodeTile<Off, kThreadsPerCta>(args, c.rec, c.batch, c.local, next);
+  if (c.coef_batch != c.batch) {
+    E::Fetch(args, c.rec.coef_slot, c.batch, c.coef);
+    c.coef_batch = c.batch;
+  }
+  const int4* from = reinterpret_cast<const int4*>(c.coef);
+  int4* to = reinterpret_cast<int4*>(next.coef);
+  to[0] = from[0];
+  to[1] = from[1];
+}
+
+// Thread 0 only: advance the cursor to the next tile and decode it.
+template <typename E, typename Off, int kThreadsPerCta>
+__device__ __forceinline__ void DecodeNext(const MapArgs& args, MapCursor& c, TileState<Off>& next) {
+  ++c.local;
+  if (c.local == args.tiles_per_batch) {
+    c.local = 0;
+    ++c.batch;
+    if (c.rec_index != 0) LoadRecord(args, 0, c);
+  }
+  while (c.local >= c.next_begin) LoadRecord(args, c.rec_index + 1, c);
+  DecodeAt<E, Off, kThreadsPerCta>(args, c, next);
+}
+
+// One persistent CTA walks a contiguous range of tiles through kMapStages
+// shared-memory stages: while tile i is written out of its stage, the loads
+// of tiles i + 1 .. i + kMapStages - 1 are in flight (one cp.async group per
+// tile), and thread 0 decodes tile i + kMapStages.  Tile states live in
+// kMapStages + 1 slots: the tile being stored, the tiles in flight and the one
+// being decoded.
+#ifndef T0B_MAP_STAGES
+#define T0B_MAP_STAGES 1
+#endif
+constexpr int kMapStages = T0B_MAP_STAGES;
+
 template <int Op>
 struct MapShape {
   static constexpr int kThreads = Op == kOpUpdate ? T0B_UPDATE_THREADS : T0B_PERMUTE_THREADS;
   static constexpr int kMinBlocks = Op == kOpUpdate ? T0B_UPDATE_MIN_BLOCKS : T0B_PERMUTE_MIN_BLOCKS;
 };
 
+__device__ __forceinline__ void CommitGroup() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+// Wait until at most kMapStages - 1 of this thread's cp.async groups are pending.
+__device__ __forceinline__ void WaitOldestGroup() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kMapStages - 1) : "memory");
+}
+
 template <int Op, typename T, typename CA, typename CB, typename Off>
 __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBlocks) MapKernel(MapArgs args) {
   using E = Emit<Op, T, CA, CB>;
   constexpr int kCta = MapShape<Op>::kThreads;
+  constexpr int kSlots = kMapStages + 1;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ TileState<Off> states[2];        // the current tile and the next one
-  __shared__ int64_t cursor[3];               // decoding thread: record, batch, tile within the batch
-  const uint32_t tile_s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
-  const uint32_t base_s = tile_s + static_cast<uint32_t>(args.tile_elems * sizeof(T));
+  __shared__ TileState<Off> states[kSlots];
+  __shared__ MapCursor cursor;                 // the decoding thread's position
+  const uint32_t smem_s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  // A stage holds the source tile and, for update, the base values after it.
+  const uint32_t tile_bytes = static_cast<uint32_t>(args.tile_elems * sizeof(T));
+  const uint32_t stage_bytes = E::kReadsBase ? 2 * tile_bytes : tile_bytes;
   const int64_t total = args.tiles_per_batch * args.batches;
   const int64_t per_cta = (total + gridDim.x - 1) / gridDim.x;
   const int64_t first = static_cast<int64_t>(blockIdx.x) * per_cta;
@@ -420,27 +568,47 @@ __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBloc
       const int64_t mid = (lo + hi + 1) >> 1;
       if (args.recs[mid].tile_begin <= local) lo = mid; else hi = mid - 1;
     }
-    cursor[0] = lo; cursor[1] = batch; cursor[2] = local;
-    DecodeTile<Off, kCta>(args, lo, batch, local, states[0]);
-    E::Fetch(args, states[0].slot, states[0].batch, states[0].coef);
+    LoadRecord(args, lo, cursor);
+    cursor.batch = batch;
+    cursor.local = local;
+    DecodeAt<E, Off, kCta>(args, cursor, states[0]);
+    for (int64_t k = 1; k < kMapStages && k < count; ++k) DecodeNext<E, Off, kCta>(args, cursor, states[k]);
   }
   __syncthreads();
+  // Prologue: the loads of tiles 0 .. kMapStages - 2.
+  for (int64_t k = 0; k + 1 < kMapStages; ++k) {
+    if (k < count) {
+      const uint32_t stage = smem_s + static_cast<uint32_t>(k) * stage_bytes;
+      LoadTile<E, T, Off, kCta>(args, states[k], stage, stage + tile_bytes);
+    }
+    CommitGroup();
+  }
   for (int64_t i = 0; i < count; ++i) {
-    const TileState<Off>& st = states[i & 1];
-    LoadTile<E, T, Off, kCta>(args, st, tile_s, base_s);
-    // While the copies fly, the decoding thread prepares the next tile.
-    if (threadIdx.x == 0 && i + 1 < count) DecodeNext<E, Off, kCta>(args, cursor, states[(i + 1) & 1]);
-    WaitAsync();
+    // Loads of tile i + kMapStages - 1 into the stage tile i - 1 released.
+    const int64_t ahead = i + kMapStages - 1;
+    if (ahead < count) {
+      const uint32_t stage = smem_s + static_cast<uint32_t>(ahead % kMapStages) * stage_bytes;
+      LoadTile<E, T, Off, kCta>(args, states[ahead % kSlots], stage, stage + tile_bytes);
+    }
+    CommitGroup();
+    // While the copies fly, the decoding thread prepares tile i + kMapStages
+    // in the slot tile i - 1 released.
+    if (threadIdx.x == 0 && i + kMapStages < count) {
+      DecodeNext<E, Off, kCta>(args, cursor, states[(i + kMapStages) % kSlots]);
+    }
+    WaitOldestGroup();
     __syncthreads();
     // Store: destination runs out of the tile, with the rule specialised per kind.
     {
+      const TileState<Off>& st = states[i % kSlots];
+      const uint32_t tile_s = smem_s + static_cast<uint32_t>(i % kMapStages) * stage_bytes;
       const E emit(st.coef);
       const bool skip = emit.SkipSource();
       T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
-      const uint32_t base_offset = base_s - tile_s;
+      const uint32_t base_offset = tile_bytes;
       auto store = [&](auto kind) {
         constexpr int K = decltype(kind)::value;
-        Walk<Off, kCta, true>(st.store, out, tile_s, [&](T* p, uint32_t s) {
+        auto element = [&](T* p, uint32_t s) {
           T v{}, old{};
           if constexpr (E::kReadsBase) {
             // Update reads both stages without a branch (measured faster); a
@@ -452,7 +620,12 @@ __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBloc
             if (!skip) v = LoadShared<T>(s);
           }
           *p = emit.template Apply<K>(v, old);
-        });
+        };
+        if (st.rect) {
+          RectDestinationRows<kCta>(st.box, out, tile_s, element);
+        } else {
+          Walk<Off, kCta, true>(st.store, out, tile_s, element);
+        }
       };
       switch (emit.Kind()) {
         case 1: store(std::integral_constant<int, 1>{}); break;
@@ -658,7 +831,12 @@ void Check(cudaError_t status, const char* what) {
   }
 }
 
-void MapTileElements(const MapRecord* recs, int64_t count, int64_t* tile, int64_t* box) {
+int64_t MapSharedBytes(int op, int64_t tile_elems, int element_bytes) {
+  const int64_t tile = tile_elems * element_bytes;
+  return (op == kOpUpdate ? 2 * tile : tile) * kMapStages;
+}
+
+void MapTileElements(const MapRecord* recs, int64_t count, int element_bytes, int64_t* tile, int64_t* box) {
   *tile = 0;
   *box = 0;
   for (int64_t i = 0; i < count; ++i) {

@@ -57,7 +57,10 @@ extern std::atomic<uint64_t> g_kernel_launches;
 void Check(cudaError_t status, const char* what);
 
 // Largest padded tile (shared-memory elements) and largest tile box over a plan's records.
-void MapTileElements(const MapRecord* recs, int64_t count, int64_t* tile, int64_t* box);
+void MapTileElements(const MapRecord* recs, int64_t count, int element_bytes, int64_t* tile, int64_t* box);
+// Dynamic shared memory of one map CTA for an operation: every pipeline stage
+// holds a staged tile (and, for update, the base values after it).
+int64_t MapSharedBytes(int op, int64_t tile_elems, int element_bytes);
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
                int smem, bool wide, cudaStream_t stream);
 void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream);

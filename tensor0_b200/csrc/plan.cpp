@@ -17,18 +17,27 @@ namespace {
 constexpr uint64_t kExtentLimit = uint64_t{1} << 30;   // per-axis extent kept in int32
 constexpr uint64_t kProofLimit = uint64_t{1} << 28;    // largest address span checked with a bitmap
 
-// Bytes of shared memory one map tile may stage (before row padding): 16 KB
-// for copy and accumulation (eight 128-thread CTAs per SM), 32 KB for update,
+// Bytes of shared memory one map tile may stage (before row padding): 48 KB
+// for copy and accumulation (four 128-thread CTAs per SM; the third box axis
+// then extends short source rows to several hundred bytes), 32 KB for update,
 // which stages the destination's base values beside it (three 256-thread CTAs
 // per SM, 64 KB each).
 #ifndef T0B_TILE_BYTES
-#define T0B_TILE_BYTES 16384
+#define T0B_TILE_BYTES 49152
 #endif
 #ifndef T0B_UPDATE_TILE_BYTES
 #define T0B_UPDATE_TILE_BYTES 32768
 #endif
 constexpr int64_t kTileBytes = T0B_TILE_BYTES;
 constexpr int64_t kUpdateTileBytes = T0B_UPDATE_TILE_BYTES;
+// Shortest X and Y tile extents walked with the fixed rectangular thread map:
+// shorter rows leave most lanes of a warp idle there, and the run walk packs
+// them instead.  The map is used for update tiles, where it measured faster
+// than the run walk; copy and accumulation measured faster with the run walk.
+#ifndef T0B_RECT_MIN_EXTENT
+#define T0B_RECT_MIN_EXTENT 32
+#endif
+constexpr int32_t kRectMinExtent = T0B_RECT_MIN_EXTENT;
 
 // Split records so every axis extent fits in int32 and at most kMaxRank axes remain.
 std::vector<Record> SplitForDevice(const Record& record) {
@@ -252,7 +261,7 @@ void SetDivisions(MapRecord& r) {
   }
 }
 
-MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int64_t tile_begin) {
+MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int64_t tile_begin, bool allow_rect) {
   MapRecord out{};
   out.src_off = record.src_off;
   out.dst_off = record.dst_off;
@@ -325,6 +334,11 @@ MapRecord MakeMapRecord(const Record& record, int64_t slot, int64_t budget, int6
   }
   if (z_axis != rank) put(2, z_axis);
   out.t[2] = static_cast<int32_t>(std::min<int64_t>(out.n[2], std::max<int64_t>(1, budget / (int64_t{out.t[0]} * out.t[1]))));
+  // The rectangular thread map covers X and Y extents up to 64 (two lanes' worth).
+  if (allow_rect && out.mode == kTranspose && out.s[1] == 1 && out.d[0] == 1 && out.t[0] >= kRectMinExtent &&
+      out.t[1] >= kRectMinExtent && out.t[0] <= 64 && out.t[1] <= 64) {
+    out.mode = kRect;
+  }
   for (int i = 0; i < 3; ++i) out.c[i] = static_cast<int32_t>(CeilDiv(out.n[i], out.t[i]));
   out.nouter = static_cast<int32_t>(rest.size());
   for (std::size_t i = 0; i < rest.size(); ++i) put(3 + static_cast<int>(i), rest[i]);
@@ -481,7 +495,8 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     Record fused = records[i];
     Canonicalize(fused, true);
     MapRecord record = MakeMapRecord(fused, record_slot[i],
-                                     (operation == 1 ? kUpdateTileBytes : kTileBytes) / element_bytes, tiles);
+                                     (operation == 1 ? kUpdateTileBytes : kTileBytes) / element_bytes, tiles,
+                                     operation == 1);
     tiles += MapTiles(record);
     plan.map_wide = plan.map_wide || NeedsWideOffsets(record);
     covered += ElementCount(records[i]);

@@ -63,7 +63,13 @@ struct alignas(16) MapRecord {
   int32_t pad2_[2];
 };
 
-enum MapMode : int32_t { kTranspose = 0, kDirect = 1 };
+// kTranspose: the general run walk of a transposing tile.  kDirect: X is
+// innermost on both sides.  kRect: a transposing tile whose X has unit
+// destination stride and Y unit source stride, both at least kRectMinExtent
+// long: walked with a fixed thread map (lanes along Y to load, along X to
+// store) and no run lists.
+enum MapMode : int32_t { kTranspose = 0, kDirect = 1, kRect = 2 };
+
 
 // Reduce-engine group of records that write the same output map.
 struct alignas(16) ReduceGroup {

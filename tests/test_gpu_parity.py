@@ -15,6 +15,7 @@ import pytest
 import torch
 
 from oracle import stride_oracle as so
+from random_layouts import random_layout
 from tensor0_b200 import _native, stride
 from tensor0_b200.structure import (ProductSector, U1Irrep, Z2Irrep, Z3Irrep, degeneracy_structure, hom,
                                     space)
@@ -83,34 +84,6 @@ def test_config_one_permute_and_add_transform_match_reference_bits():
     w = add_transform(base, x, ((1, 0), (3, 2)), alpha=1.0, beta=0.5, inplace=True)
     assert w.data.data_ptr() == base.data.data_ptr()
     assert digest(host(w.data)) == golden["add_transform_sha256"]
-
-
-def random_layout(rng, source_size, output_size, records, max_rank=4, max_extent=6):
-    out, cursor = [], 0
-    for _ in range(records):
-        rank = int(rng.integers(1, max_rank + 1))
-        shape = tuple(int(n) for n in rng.integers(1, max_extent, size=rank))
-        count = int(np.prod(shape))
-        if cursor + count > output_size:
-            break
-        if count > source_size:
-            continue
-        dst = stride.contiguous_strides(shape)
-        perm = rng.permutation(rank)
-        src_shape = tuple(shape[p] for p in perm)
-        src_contig = stride.contiguous_strides(src_shape)
-        sstr = [0] * rank
-        for i, p in enumerate(perm):
-            sstr[p] = src_contig[i]
-        sign = rng.choice([-1, 1], size=rank)
-        sstr = [int(s * g) for s, g in zip(sstr, sign)]
-        soff = int(rng.integers(0, source_size - count + 1))
-        soff += sum((n - 1) * (-s) for n, s in zip(shape, sstr) if s < 0)
-        if soff + sum((n - 1) * s for n, s in zip(shape, sstr) if s > 0) >= source_size:
-            continue
-        out.append(stride.AffineRecord(shape, tuple(sstr), soff, dst, cursor))
-        cursor += count + int(rng.integers(0, 3))
-    return out
 
 
 def sample(rng, dtype, shape):
@@ -290,3 +263,37 @@ def test_engine_launches_are_counted():
     before = stride.kernel_launches()
     test_config_one_permute_and_add_transform_match_reference_bits()
     assert stride.kernel_launches() >= before + 3
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_rectangular_tiles_with_edges(dtype):
+    """Transposes with unit strides on both sides and X / Y extents from 32 to
+    130: the fixed-map rectangular tiles, including edge tiles along X (64 + 1,
+    64 + 66), ragged Y and several Z slices per tile."""
+    rng = np.random.default_rng(131)
+    shapes = [(32, 32), (64, 64), (65, 40), (130, 33), (40, 3, 97), (33, 7, 50), (70, 2, 70)]
+    records, src_off, dst_off = [], 0, 0
+    for shape in shapes:
+        # Source row-major, destination with the axis order reversed: the
+        # source's innermost axis is the destination's outermost.
+        dst = stride.contiguous_strides(tuple(reversed(shape)))[::-1]
+        src = stride.contiguous_strides(shape)
+        records.append(stride.AffineRecord(shape, tuple(src), src_off, tuple(dst), dst_off))
+        count = int(np.prod(shape))
+        src_off += count + 3
+        dst_off += count + 1
+    words = stride.encode_layout(records, source_size=src_off, output_size=dst_off)
+    x, base = sample(rng, dtype, (2, src_off)), sample(rng, dtype, (2, dst_off))
+    eb = np.dtype(dtype).itemsize
+    real = np.float32 if dtype in (np.float32, np.complex64) else np.float64
+    copy = stride.Plan(_native.OP_COPY, words, element_bytes=eb)
+    assert np.array_equal(bits(host(stride.execute_copy(cuda(x), copy))), bits(so.copy(words, x)))
+    coefficients = np.array([1.0, -0.5, 1.0, 2.0, 0.0, 1.0, 3.0], real)
+    acc = stride.Plan(_native.OP_ACCUMULATION, words, element_bytes=eb, coefficient_records=np.arange(len(records)),
+                      outputs_disjoint=True)
+    got = host(stride.execute_accumulation(cuda(x), acc, torch.from_numpy(coefficients)))
+    assert np.array_equal(bits(got), bits(so.accumulation(words, x, list(coefficients), np.arange(len(records)))))
+    update = stride.Plan(_native.OP_UPDATE, words, element_bytes=eb)
+    for alpha, beta in ((1.0, 1.0), (1.0, 0.0), (-2.0, 0.5), (0.0, 1.0)):
+        got = host(stride.execute_update(cuda(x), cuda(base), alpha, beta, update))
+        assert np.array_equal(bits(got), bits(so.update(words, x, base, real(alpha), real(beta)))), (alpha, beta)

@@ -12,6 +12,7 @@ import pytest
 
 from oracle import ref, stride_oracle as so
 from tensor0_b200 import stride
+from random_layouts import random_reduction_layout
 from tensor0_b200.structure import U1Irrep, degeneracy_structure, hom, space
 from tensor0_b200.tensor_map import permute_plan
 
@@ -121,45 +122,6 @@ def test_sector_gemm_oracle_is_blockwise_matmul():
     np.testing.assert_allclose(out[:12].reshape(3, 4), left[:15].reshape(3, 5) @ right[:20].reshape(5, 4))
     assert np.all(out[12:16] == 0)
     np.testing.assert_allclose(out[16:19], (left[15:17].reshape(1, 2) @ right[20:26].reshape(2, 3)).reshape(-1))
-
-
-def random_reduction_layout(rng, source_size, records):
-    """Random reduction records: a permuted strided box of the source per
-    record, some axes summed; outputs either a fresh contiguous region or the
-    region of an earlier record with the same open shape (contributions add)."""
-    out, shapes, roles, regions, cursor = [], [], [], [], 0
-    for _ in range(records):
-        rank = int(rng.integers(1, 5))
-        shape = tuple(int(n) for n in rng.integers(1, 5, size=rank))
-        role = tuple(bool(r) for r in rng.integers(0, 2, size=rank))
-        count = int(np.prod(shape))
-        if count > source_size:
-            continue
-        perm = rng.permutation(rank)
-        src_contig = stride.contiguous_strides(tuple(shape[p] for p in perm))
-        sstr = [0] * rank
-        for i, p in enumerate(perm):
-            sstr[p] = src_contig[i]
-        sign = rng.choice([-1, 1], size=rank)
-        sstr = [int(s * g) for s, g in zip(sstr, sign)]
-        soff = int(rng.integers(0, source_size - count + 1))
-        soff += sum((n - 1) * (-s) for n, s in zip(shape, sstr) if s < 0)
-        if soff + sum((n - 1) * s for n, s in zip(shape, sstr) if s > 0) >= source_size:
-            continue
-        open_shape = tuple(n for n, r in zip(shape, role) if not r)
-        reuse = [d for s, d in regions if s == open_shape]
-        if reuse and rng.random() < 0.5:
-            dst_off = int(rng.choice(reuse))
-        else:
-            dst_off = cursor
-            regions.append((open_shape, cursor))
-            cursor += int(np.prod(open_shape)) + int(rng.integers(0, 2))
-        open_strides = iter(stride.contiguous_strides(open_shape))
-        dstr = tuple(1 if r else next(open_strides) for r in role)
-        out.append(stride.AffineRecord(shape, tuple(sstr), soff, dstr, dst_off))
-        shapes.append(tuple(1 if r else n for n, r in zip(shape, role)))
-        roles.append(role)
-    return out, shapes, roles, max(cursor, 1)
 
 
 @needs_ref
