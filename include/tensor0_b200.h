@@ -59,6 +59,12 @@ extern "C" {
  * strides fit 32 bits (the planner selects them by itself for records whose
  * tile spans exceed 2^31 elements); results are identical. */
 #define T0B_PLAN_WIDE_OFFSETS 2u
+/* Accumulation and reduction plans: read the complex conjugate of every
+ * source element (real storage is unaffected).  This fuses the conjugation
+ * the reference applies to a source before an adjoint-destination transform
+ * (operations/transforms.py:190-259: jnp.conj, then the strided accumulation)
+ * into the same pass; conjugation is exact, so results are identical. */
+#define T0B_PLAN_CONJUGATE_SOURCE 4u
 
 typedef struct t0b_plan t0b_plan;
 

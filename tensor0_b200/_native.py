@@ -17,6 +17,7 @@ S32, F32, F64, C64, C128 = 4, 11, 12, 15, 18
 OP_COPY, OP_UPDATE, OP_ACCUMULATION, OP_REDUCTION = 0, 1, 3, 4
 PLAN_OUTPUTS_DISJOINT = 1
 PLAN_WIDE_OFFSETS = 2
+PLAN_CONJUGATE_SOURCE = 4
 
 c_i64p = ctypes.POINTER(ctypes.c_int64)
 

@@ -138,6 +138,7 @@ void RunMap(const t0b_plan* plan, int op, int32_t dtype, int32_t ca_dtype, int32
   args.ca_count = ca_count;
   args.cb = cb;
   args.cb_count = cb_count;
+  args.conjugate = plan->plan.conjugate ? 1 : 0;
   t0b::LaunchMap(op, dtype, ca_dtype, cb_dtype, args, plan->map_smem, plan->plan.map_wide, stream);
 }
 
@@ -164,6 +165,7 @@ void RunReduce(const t0b_plan* plan, int32_t dtype, int32_t ca_dtype, const void
     args.out_size = static_cast<int64_t>(plan->plan.output_size);
     args.ca = ca;
     args.ca_count = ca_count;
+    args.conjugate = plan->plan.conjugate ? 1 : 0;
     t0b::LaunchReduce(dtype, ca_dtype, args, stream);
   }
 }

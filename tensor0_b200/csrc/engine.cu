@@ -604,6 +604,7 @@ __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBloc
       const uint32_t tile_s = smem_s + static_cast<uint32_t>(i % kMapStages) * stage_bytes;
       const E emit(st.coef);
       const bool skip = emit.SkipSource();
+      const bool conjugate = args.conjugate != 0;
       T* __restrict__ out = static_cast<T*>(args.out) + st.dof;
       const uint32_t base_offset = tile_bytes;
       auto store = [&](auto kind) {
@@ -618,6 +619,11 @@ __global__ void __launch_bounds__(MapShape<Op>::kThreads, MapShape<Op>::kMinBloc
             old = LoadShared<T>(s + base_offset);
           } else {
             if (!skip) v = LoadShared<T>(s);
+            if constexpr (Op == kOpAccumulation) {
+              if constexpr (Elem<T>::kComplex) {
+                if (conjugate) v.y = -v.y;
+              }
+            }
           }
           *p = emit.template Apply<K>(v, old);
         };
@@ -712,7 +718,10 @@ __global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
           rest /= n;
           off += i * rec.s[mr + a];
         }
-        const T value = src[at + off];
+        T value = src[at + off];
+        if constexpr (Elem<T>::kComplex) {
+          if (args.conjugate) value.y = -value.y;
+        }
         acc = Add(acc, one ? value : Scale(c, value));
       }
     }

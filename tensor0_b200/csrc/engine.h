@@ -32,6 +32,7 @@ struct MapArgs {
   int64_t ca_count;
   const void* cb;      // update: beta
   int64_t cb_count;
+  int conjugate;       // accumulation: read conj(source) (complex storage)
 };
 
 struct ReduceArgs {
@@ -49,6 +50,7 @@ struct ReduceArgs {
   int64_t out_size;
   const void* ca;
   int64_t ca_count;
+  int conjugate;                    // read conj(source) (complex storage)
 };
 
 extern std::atomic<uint64_t> g_kernel_launches;

@@ -398,6 +398,9 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
   if (!summing && coefficient_count != 0) {
     throw InvalidArgument("copy and update plans take no coefficient records");
   }
+  if (!summing && (flags & 4u) != 0) {
+    throw InvalidArgument("source conjugation is supported for accumulation and reduction plans");
+  }
   std::vector<int64_t> slot(layout.records.size(), -1);
   int64_t previous = -1;
   for (std::size_t i = 0; i < coefficient_count; ++i) {
@@ -591,6 +594,7 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
   }
 
   if ((flags & 2u) != 0) plan.map_wide = true;
+  plan.conjugate = (flags & 4u) != 0;
   plan.has_map = !map_records.empty();
   plan.has_reduce = !groups.empty();
   plan.map_tiles = static_cast<uint64_t>(tiles);

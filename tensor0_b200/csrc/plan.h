@@ -133,6 +133,7 @@ struct Plan {
   bool has_map = false;
   bool has_reduce = false;
   bool map_wide = false;         // some tile needs 64-bit in-tile offsets
+  bool conjugate = false;        // read the complex conjugate of the source
   uint64_t map_tiles = 0;
   uint64_t tasks = 0;
   uint64_t owners = 0;

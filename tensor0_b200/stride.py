@@ -124,7 +124,8 @@ class Plan:
     """Prepared state of one operation over one layout (the reference's instantiate)."""
 
     def __init__(self, operation: int, words: np.ndarray, *, element_bytes: int,
-                 coefficient_records=(), outputs_disjoint: bool = False, wide_offsets: bool = False):
+                 coefficient_records=(), outputs_disjoint: bool = False, wide_offsets: bool = False,
+                 conjugate_source: bool = False):
         self._lib = _native.lib()
         words = np.ascontiguousarray(words, dtype=np.int64)
         records = np.ascontiguousarray(np.asarray(coefficient_records, dtype=np.int64))
@@ -134,7 +135,8 @@ class Plan:
             operation, words.ctypes.data_as(_native.c_i64p), words.size,
             records.ctypes.data_as(_native.c_i64p) if records.size else None, records.size,
             element_bytes, (_native.PLAN_OUTPUTS_DISJOINT if outputs_disjoint else 0)
-            | (_native.PLAN_WIDE_OFFSETS if wide_offsets else 0),
+            | (_native.PLAN_WIDE_OFFSETS if wide_offsets else 0)
+            | (_native.PLAN_CONJUGATE_SOURCE if conjugate_source else 0),
             ctypes.byref(handle), err, len(err))
         _native.check(status, err)
         self._handle = handle

@@ -22,9 +22,21 @@ spaces plan in seconds):
   start + row_offset * col_dim + col_offset;
 * HomSpace.permute — space/hom.rs:202-231 (legs moving sides are dualised);
 * abelian tree braiding — transform/tree_transformers.rs:216-242 with
-  fusion_tree/braiding_ops.rs:129-189: a pair maps to the pair with the
-  permuted uncoupled sectors; for bosonic families the coefficient is 1;
-* trace transformer — transform/trace_transformers.rs:57-84 and 214-246.
+  fusion_tree/braiding_ops.rs:18-46 and 129-189: a pair maps to the pair with
+  the permuted uncoupled sectors.  The coefficient is the product of
+  R-symbols over the inversions of the linearized permutation
+  (fusion_tree/auxiliary.rs:82-141: codomain legs, then the domain legs in
+  reverse); the repartition factors (duality_ops.rs:23-50, 372-382) are 1 for
+  these families, whose F-, B-symbols and Frobenius-Schur phases are 1.  R is
+  -1 exactly when both sectors have odd fermion parity
+  (sector/fermion_parity.rs:79-88), so bosonic families have coefficient 1;
+* twist factors — transform/reweighting.rs:60-99 (product of the twists of
+  the selected legs' uncoupled sectors, theta = -1 for odd parity);
+* flip — space/graded.rs:89-100, space/hom.rs:156-200 and
+  fusion_tree/braiding_ops.rs:84-127;
+* trace transformer — transform/trace_transformers.rs:57-84 and 214-246,
+  with the coefficient of trace_coefficient (the twists of the non-dual
+  traced legs; the tail tree's first sector is the open head's coupled one).
 """
 
 from __future__ import annotations
@@ -39,7 +51,7 @@ __all__ = [
     "SectorType", "U1Irrep", "Z2Irrep", "Z3Irrep", "Z4Irrep", "ZNIrrep", "FermionParity",
     "ProductSector", "GradedSpace", "HomSpace", "space", "hom", "SectorStructure",
     "DegeneracyStructure", "sector_structure", "degeneracy_structure", "tree_permuter",
-    "trace_transformer", "AbelianTransform",
+    "trace_transformer", "AbelianTransform", "twist_factors", "flip_transform", "adjoint_transform",
 ]
 
 
@@ -111,6 +123,19 @@ class SectorType:
                 values[..., c] %= 2
         return values
 
+    def parity(self, a: np.ndarray) -> np.ndarray:
+        """Per fermion-parity component, whether the sector is odd: [..., n_fp] bools."""
+        a = np.asarray(a, dtype=np.int64)
+        columns = [c for c, (kind, _) in enumerate(self.components) if kind == "FP"]
+        if not columns:
+            return np.zeros((*a.shape[:-1], 0), bool)
+        return (a[..., columns] % 2) == 1
+
+    def twist(self, a: np.ndarray) -> np.ndarray:
+        """Sector twists theta (product over components; -1 for odd parity)."""
+        odd = self.parity(a)
+        return np.where(odd.sum(axis=-1) % 2 == 1, -1.0, 1.0)
+
     def sort_index(self, a: np.ndarray) -> np.ndarray:
         """Per-component canonical indices (u1.rs:123-130; zn / parity: value)."""
         a = np.asarray(a, dtype=np.int64)
@@ -178,6 +203,17 @@ class GradedSpace:
 
     def dual(self) -> "GradedSpace":
         return GradedSpace(self.sector_type, self.stored, self.dims, not self.is_dual)
+
+    def flip(self) -> "GradedSpace":
+        """Stored sectors dualised and re-sorted, duality toggled: the visible
+        sectors stay the same (space/graded.rs:89-100)."""
+        st = self.sector_type
+        if not self.stored:
+            return GradedSpace(st, self.stored, self.dims, not self.is_dual)
+        duals = st.dual(np.array(self.stored, dtype=np.int64).reshape(-1, st.width))
+        order = st.order(duals)
+        return GradedSpace(st, tuple(tuple(int(v) for v in duals[i]) for i in order),
+                           tuple(self.dims[i] for i in order), not self.is_dual)
 
     @cached_property
     def visible(self) -> np.ndarray:
@@ -253,6 +289,26 @@ class HomSpace:
     @property
     def dims(self) -> tuple[int, ...]:
         return tuple(leg.dim for leg in (*self.codomain, *self.domain))
+
+    def flip(self, indices) -> "HomSpace":
+        """The selected visible legs flipped (space/hom.rs:156-200)."""
+        chosen = set(_normalize_indices(indices, self.numind, "flip"))
+        codomain = tuple(leg.flip() if i in chosen else leg for i, leg in enumerate(self.codomain))
+        domain = tuple(leg.flip() if self.numout + j in chosen else leg for j, leg in enumerate(self.domain))
+        return HomSpace(codomain, domain)
+
+
+def _normalize_indices(indices, rank: int, what: str) -> tuple[int, ...]:
+    values = (indices,) if isinstance(indices, int) else tuple(indices)
+    out = []
+    for index in values:
+        index = int(index)
+        if not 0 <= index < rank:
+            raise ValueError(f"{what} visible index {index} is out of range for rank {rank}")
+        if index in out:
+            raise ValueError(f"{what} visible indices must be unique")
+        out.append(index)
+    return tuple(out)
 
 
 def hom(codomain, domain) -> HomSpace:
@@ -484,26 +540,120 @@ def _lookup(dst: HomSpace, rows: np.ndarray, cols: np.ndarray) -> np.ndarray:
     return found
 
 
+def _pair_sectors(space: HomSpace, ss: SectorStructure) -> np.ndarray:
+    """Uncoupled (visible) sectors of every pair: [P, numind, width], codomain
+    legs then domain legs."""
+    legs = (*space.codomain, *space.domain)
+    width = space.sector_type.width
+    indices = np.concatenate([ss.pair_row, ss.pair_col], axis=1)
+    if not legs:
+        return np.zeros((ss.pair_count, 0, width), np.int64)
+    return np.stack([leg.visible[indices[:, i]] for i, leg in enumerate(legs)], axis=1)
+
+
+def _braid_signs(space: HomSpace, ss: SectorStructure, p_codomain, p_domain) -> np.ndarray:
+    """Product of R-symbols over the inversions of the linearized permutation
+    (braiding_ops.rs:129-189): -1 per inverted pair of legs whose sectors are
+    both odd in a fermion-parity component."""
+    n1, n2 = space.numout, space.numin
+    count = ss.pair_count
+    if space.sector_type.bosonic:
+        return np.ones(count, np.float64)
+
+    def linear(index: int) -> int:
+        return index if index < n1 else n1 + n2 - 1 - (index - n1)
+
+    permutation = [linear(i) for i in (*p_codomain, *reversed(p_domain))]
+    # The full outgoing tree lists the codomain legs, then the domain legs in reverse.
+    visible = _pair_sectors(space, ss)
+    order = list(range(n1)) + [n1 + n2 - 1 - k for k in range(n2)]
+    odd = space.sector_type.parity(visible[:, order, :]) if count else np.zeros((0, n1 + n2, 0), bool)
+    flips = np.zeros(count, np.int64)
+    for i in range(len(permutation)):
+        for j in range(i):
+            if permutation[j] > permutation[i]:
+                both = odd[:, permutation[j], :] & odd[:, permutation[i], :]
+                flips += both.sum(axis=1)
+    return np.where(flips % 2 == 1, -1.0, 1.0)
+
+
 def tree_permuter(src: HomSpace, p_codomain, p_domain) -> tuple[HomSpace, AbelianTransform]:
     """Abelian tree permuter (tree_transformers.rs:95-173 via braid_pair).
 
     The destination pair of a source pair carries the same per-leg sector
     positions, permuted (a leg moving sides keeps its position in the dualised
-    space's visible list).  Bosonic families have coefficient 1.
+    space's visible list).  The coefficient is +-1: the fermionic braid sign.
     """
     p_codomain, p_domain = tuple(p_codomain), tuple(p_domain)
     dst = src.permute(p_codomain, p_domain)
-    if not src.sector_type.bosonic:
-        raise NotImplementedError("fermionic braiding coefficients are not planned by this build")
     ss = sector_structure(src)
     legs = np.concatenate([ss.pair_row, ss.pair_col], axis=1)
-    perm = list(p_codomain + p_domain)
     rows = legs[:, list(p_codomain)] if p_codomain else np.zeros((len(legs), 0), np.int64)
     cols = legs[:, list(p_domain)] if p_domain else np.zeros((len(legs), 0), np.int64)
-    del perm
     dst_index = _lookup(dst, rows, cols)
     n = ss.pair_count
-    return dst, AbelianTransform(np.arange(n, dtype=np.int64), dst_index, np.ones(n, np.float64))
+    return dst, AbelianTransform(np.arange(n, dtype=np.int64), dst_index,
+                                 _braid_signs(src, ss, p_codomain, p_domain))
+
+
+def twist_factors(space: HomSpace, indices, inv: bool = False) -> np.ndarray | None:
+    """Per-pair twist factors for the selected visible legs, or None when all
+    are 1 (reweighting.rs:60-99).  Abelian twists are +-1, their own inverse."""
+    chosen = _normalize_indices(indices, space.numind, "twist")
+    del inv
+    if not chosen or space.sector_type.bosonic:
+        return None
+    ss = sector_structure(space)
+    visible = _pair_sectors(space, ss)
+    factors = np.ones(ss.pair_count, np.float64)
+    for index in chosen:
+        factors *= space.sector_type.twist(visible[:, index, :])
+    return None if np.all(factors == 1.0) else factors
+
+
+def flip_transform(src: HomSpace, indices, inv: bool = False) -> tuple[HomSpace, AbelianTransform]:
+    """Flip the selected visible legs (braiding_ops.rs:84-127): every pair maps
+    to the pair with the same visible sectors in the flipped space; a codomain
+    leg contributes theta when its duality differs from `inv`, a domain leg when
+    it equals `inv` (the Frobenius-Schur phases are 1 for these families)."""
+    chosen = _normalize_indices(indices, src.numind, "flip")
+    dst = src.flip(chosen)
+    ss = sector_structure(src)
+    legs_src = (*src.codomain, *src.domain)
+    legs_dst = (*dst.codomain, *dst.domain)
+    indices_src = np.concatenate([ss.pair_row, ss.pair_col], axis=1)
+    mapped = indices_src.copy()
+    visible = _pair_sectors(src, ss)
+    factors = np.ones(ss.pair_count, np.float64)
+    st = src.sector_type
+    for index in chosen:
+        # Position of the same visible sector in the flipped leg's stored order.
+        target = {tuple(int(v) for v in sector): k for k, sector in enumerate(legs_dst[index].visible)}
+        mapped[:, index] = [target[tuple(int(v) for v in sector)] for sector in legs_src[index].visible[indices_src[:, index]]]
+        was_dual = legs_src[index].is_dual
+        applies = (was_dual != inv) if index < src.numout else (was_dual == inv)
+        if applies:
+            factors *= st.twist(visible[:, index, :])
+    dst_index = _lookup(dst, mapped[:, :src.numout], mapped[:, src.numout:])
+    return dst, AbelianTransform(np.arange(ss.pair_count, dtype=np.int64), dst_index, factors)
+
+
+def adjoint_transform(src: HomSpace, p_codomain, p_domain) -> tuple[HomSpace, AbelianTransform, tuple[int, ...]]:
+    """The adjoint destination of a permutation (operations/transforms.py:190-259):
+    the parent space permute(src, p), the destination hom(parent.domain,
+    parent.codomain), and every source pair sent to the swapped parent pair.
+    Returns the destination, the transform (coefficients of the permutation,
+    real, so equal to their conjugates) and the source axis order of the
+    destination's legs."""
+    parent, transform = tree_permuter(src, p_codomain, p_domain)
+    dst = HomSpace(parent.domain, parent.codomain)
+    ps = sector_structure(parent)
+    rows = ps.pair_col[transform.dst]
+    cols = ps.pair_row[transform.dst]
+    dst_index = _lookup(dst, rows, cols)
+    axes = tuple(p_codomain) + tuple(p_domain)
+    axes = axes[len(p_codomain):] + axes[:len(p_codomain)]
+    return dst, AbelianTransform(transform.src, dst_index, transform.coeff), axes
 
 
 def trace_transformer(canonical: HomSpace, dst: HomSpace, basis: AbelianTransform) -> AbelianTransform:
@@ -533,4 +683,12 @@ def trace_transformer(canonical: HomSpace, dst: HomSpace, basis: AbelianTransfor
     cc = coupled(canonical.domain[:ni], head_c)
     keep &= np.all(cr == cc, axis=1)
     dst_index = _lookup(dst, head_r[keep], head_c[keep])
-    return AbelianTransform(basis.src[keep], dst_index, basis.coeff[keep])
+    coefficient = basis.coeff[keep].copy()
+    # trace_coefficient: the tail tree (split, basic_ops) starts with the open
+    # head's coupled sector, then the traced legs; every traced leg that is
+    # not dual contributes its twist (quantum dimensions are 1).
+    for k in range(tail_r.shape[1]):
+        leg = canonical.codomain[no + k]
+        if not leg.is_dual:
+            coefficient *= st.twist(leg.visible[tail_r[keep][:, k]])
+    return AbelianTransform(basis.src[keep], dst_index, coefficient)

@@ -15,7 +15,15 @@ Mirrors the reference's public operations for abelian sector families:
   call evaluates every contribution;
 * ``tensorcontract`` — primitives.py:307-430: operand permutes chosen by the
   reference's copy-cost rule (primitives.py:147-234), per-sector GEMMs
-  (linalg.py:533-566) and the output permute.
+  (linalg.py:533-566) and the output permute; conjugated operands are
+  prepared in one conjugating pass into their adjoint destination
+  (primitives.py:288-304 with transforms.py:190-259), and the right operand's
+  dual contracted legs are twisted (primitives.py:422-428) inside its permute;
+* ``adjoint`` / ``permute_adjoint`` — tensor_map.py:503-515 and
+  transforms.py:190-259: one conjugating accumulation into hom(domain,
+  codomain);
+* ``twist`` / ``flip`` — transforms.py:275-373: one accumulation with the
+  per-sub-block +-1 factors.
 
 Storage is a CUDA tensor ``[*batch, total_dim]``; every operation is computed
 by the sm_100a engine.
@@ -32,11 +40,12 @@ import torch
 
 from . import stride
 from . import _native
-from .structure import (AbelianTransform, HomSpace, degeneracy_structure, hom, sector_structure,
-                        trace_transformer, tree_permuter)
+from .structure import (AbelianTransform, HomSpace, adjoint_transform, degeneracy_structure, flip_transform, hom,
+                        sector_structure, trace_transformer, tree_permuter, twist_factors)
 
 __all__ = ["TensorMap", "random_normal", "permute", "add_transform", "tensortrace", "tensorcontract",
-           "PermutePlan", "permute_plan", "trace_plan", "contract_plan"]
+           "adjoint", "permute_adjoint", "twist", "flip", "PermutePlan", "permute_plan", "adjoint_plan",
+           "twist_plan", "flip_plan", "trace_plan", "contract_plan"]
 
 _ELEMENT_BYTES = {torch.float32: 4, torch.float64: 8, torch.complex64: 8, torch.complex128: 16}
 
@@ -73,6 +82,10 @@ class TensorMap:
             out.append((tuple(int(x) for x in ss.blocksectors[b]), self.data[..., start:start + r * c].reshape(
                 *self.data.shape[:-1], r, c)))
         return tuple(out)
+
+    def adjoint(self) -> "TensorMap":
+        """hom(domain, codomain) with every block conjugate-transposed."""
+        return adjoint(self)
 
     def add(self, other: "TensorMap", alpha=1, beta=1) -> "TensorMap":
         """alpha * self + beta * other (tensor_map.py:434-455)."""
@@ -127,6 +140,7 @@ class PermutePlan:
     dst_strides: np.ndarray
     dst_offsets: np.ndarray
     perm: tuple = ()
+    conjugate: bool = False
     _plans: dict = None
 
     @property
@@ -138,26 +152,29 @@ class PermutePlan:
         return degeneracy_structure(self.dst).total_dim
 
     def engine_plan(self, operation: int, dtype: torch.dtype) -> stride.Plan:
-        key = (operation, _ELEMENT_BYTES[dtype])
+        key = (operation, _ELEMENT_BYTES[dtype], self.conjugate and dtype.is_complex)
         if self._plans is None:
             self._plans = {}
         plan = self._plans.get(key)
         if plan is None:
             records = np.arange(len(self.transform.src)) if operation == _native.OP_ACCUMULATION else ()
             plan = stride.Plan(operation, self.words, element_bytes=_ELEMENT_BYTES[dtype],
-                               coefficient_records=records, outputs_disjoint=self.outputs_disjoint)
+                               coefficient_records=records, outputs_disjoint=self.outputs_disjoint,
+                               conjugate_source=self.conjugate and dtype.is_complex)
             self._plans[key] = plan
         return plan
 
 
-@lru_cache(maxsize=256)
-def permute_plan(src: HomSpace, p_codomain: tuple[int, ...], p_domain: tuple[int, ...]) -> PermutePlan:
-    """Tree permuter + affine records (_tensor_ops.py:17-87), vectorised."""
-    dst, transform = tree_permuter(src, p_codomain, p_domain)
+def _affine_plan(src: HomSpace, dst: HomSpace, transform: AbelianTransform, perm: tuple[int, ...],
+                 conjugate: bool = False) -> PermutePlan:
+    """Affine records of an abelian transform (_tensor_ops.py:17-87), vectorised:
+    source sub-block transform.src read along the source axes `perm`, written
+    to destination sub-block transform.dst."""
     sd, dd = degeneracy_structure(src), degeneracy_structure(dst)
-    perm = list(p_codomain + p_domain)
-    shape = sd.sizes[transform.src][:, perm] if perm else np.zeros((len(transform.src), 0), np.int64)
-    sstr = sd.strides[transform.src][:, perm] if perm else np.zeros((len(transform.src), 0), np.int64)
+    perm = list(perm)
+    count = len(transform.src)
+    shape = sd.sizes[transform.src][:, perm] if perm else np.zeros((count, 0), np.int64)
+    sstr = sd.strides[transform.src][:, perm] if perm else np.zeros((count, 0), np.int64)
     if not np.array_equal(shape, dd.sizes[transform.dst]):
         raise ValueError("Abelian tree transform subblock shapes are inconsistent")
     disjoint = np.unique(transform.dst).size == transform.dst.size
@@ -165,7 +182,41 @@ def permute_plan(src: HomSpace, p_codomain: tuple[int, ...], p_domain: tuple[int
                                         dd.offsets[transform.dst], source_size=sd.total_dim,
                                         output_size=dd.total_dim)
     return PermutePlan(src, dst, words, transform, bool(disjoint), shape, sstr, sd.offsets[transform.src],
-                       dd.strides[transform.dst], dd.offsets[transform.dst], tuple(perm))
+                       dd.strides[transform.dst], dd.offsets[transform.dst], tuple(perm), conjugate=conjugate)
+
+
+@lru_cache(maxsize=256)
+def permute_plan(src: HomSpace, p_codomain: tuple[int, ...], p_domain: tuple[int, ...]) -> PermutePlan:
+    """Tree permuter + affine records (_tensor_ops.py:17-87)."""
+    dst, transform = tree_permuter(src, p_codomain, p_domain)
+    return _affine_plan(src, dst, transform, tuple(p_codomain + p_domain))
+
+
+@lru_cache(maxsize=256)
+def adjoint_plan(src: HomSpace, p_codomain: tuple[int, ...], p_domain: tuple[int, ...]) -> PermutePlan:
+    """The permutation's adjoint destination (transforms.py:190-259): conjugated
+    source, destination hom(parent.domain, parent.codomain), coefficients the
+    conjugated (real) tree coefficients."""
+    dst, transform, axes = adjoint_transform(src, p_codomain, p_domain)
+    return _affine_plan(src, dst, transform, axes, conjugate=True)
+
+
+@lru_cache(maxsize=256)
+def twist_plan(src: HomSpace, indices: tuple[int, ...], inv: bool = False) -> PermutePlan | None:
+    """Per-sub-block twist factors (transforms.py:275-322), or None when trivial."""
+    factors = twist_factors(src, indices, inv)
+    if factors is None:
+        return None
+    n = len(factors)
+    transform = AbelianTransform(np.arange(n, dtype=np.int64), np.arange(n, dtype=np.int64), factors)
+    return _affine_plan(src, src, transform, tuple(range(src.numind)))
+
+
+@lru_cache(maxsize=256)
+def flip_plan(src: HomSpace, indices: tuple[int, ...], inv: bool = False) -> PermutePlan:
+    """Flip of the selected visible legs (transforms.py:325-373)."""
+    dst, transform = flip_transform(src, indices, inv)
+    return _affine_plan(src, dst, transform, tuple(range(src.numind)))
 
 
 def _normalize_p(space: HomSpace, p) -> tuple[tuple[int, ...], tuple[int, ...]]:
@@ -175,17 +226,57 @@ def _normalize_p(space: HomSpace, p) -> tuple[tuple[int, ...], tuple[int, ...]]:
     return p_codomain, p_domain
 
 
+def _run(tensor: TensorMap, plan: PermutePlan, coefficients=None) -> TensorMap:
+    """One accumulation of the plan's records over the tensor's storage."""
+    engine = plan.engine_plan(_native.OP_ACCUMULATION, tensor.data.dtype)
+    real = torch.float32 if tensor.data.dtype in (torch.float32, torch.complex64) else torch.float64
+    values = plan.transform.coeff if coefficients is None else coefficients
+    out = stride.execute_accumulation(tensor.data.contiguous(), engine, _device_constant(values, real, tensor.data.device))
+    return TensorMap(plan.dst, out)
+
+
+def _is_identity_p(space: HomSpace, p_codomain, p_domain) -> bool:
+    return tuple(p_codomain) == tuple(range(space.numout)) and tuple(p_domain) == tuple(range(space.numout, space.numind))
+
+
 def permute(tensor: TensorMap, p) -> TensorMap:
     """permute(t, ((1, 0), (3, 2))) — one accumulation call (transforms.py:32-63)."""
     p_codomain, p_domain = _normalize_p(tensor.space, p)
-    if p_codomain == tuple(range(tensor.numout)) and p_domain == tuple(range(tensor.numout, tensor.numind)):
+    if _is_identity_p(tensor.space, p_codomain, p_domain):
         return tensor
-    plan = permute_plan(tensor.space, p_codomain, p_domain)
-    engine = plan.engine_plan(_native.OP_ACCUMULATION, tensor.data.dtype)
-    real = torch.float32 if tensor.data.dtype in (torch.float32, torch.complex64) else torch.float64
-    coefficients = _device_constant(plan.transform.coeff, real, tensor.data.device)
-    out = stride.execute_accumulation(tensor.data.contiguous(), engine, coefficients)
-    return TensorMap(plan.dst, out)
+    return _run(tensor, permute_plan(tensor.space, p_codomain, p_domain))
+
+
+def permute_adjoint(tensor: TensorMap, p) -> TensorMap:
+    """adjoint(permute(t, p)) in one conjugating accumulation
+    (transforms.py:190-259, _permute_to_adjoint_destination)."""
+    p_codomain, p_domain = _normalize_p(tensor.space, p)
+    return _run(tensor, adjoint_plan(tensor.space, p_codomain, p_domain))
+
+
+def adjoint(tensor: TensorMap) -> TensorMap:
+    """t† in hom(domain, codomain): every block conjugate-transposed
+    (tensor/tensor_map.py:503-515)."""
+    return permute_adjoint(tensor, (tuple(range(tensor.numout)), tuple(range(tensor.numout, tensor.numind))))
+
+
+def twist(tensor: TensorMap, indices, inv: bool = False) -> TensorMap:
+    """twist(t, indices) (transforms.py:275-322): the selected legs' twists per sub-block."""
+    if not isinstance(inv, bool):
+        raise TypeError("twist() requires inv to be a bool")
+    chosen = (indices,) if isinstance(indices, int) else tuple(int(i) for i in indices)
+    plan = twist_plan(tensor.space, chosen, inv)
+    return tensor if plan is None else _run(tensor, plan)
+
+
+def flip(tensor: TensorMap, indices, inv: bool = False) -> TensorMap:
+    """flip(t, indices) (transforms.py:325-373)."""
+    if not isinstance(inv, bool):
+        raise TypeError("flip() requires inv to be a bool")
+    chosen = (indices,) if isinstance(indices, int) else tuple(int(i) for i in indices)
+    if not chosen:
+        return tensor
+    return _run(tensor, flip_plan(tensor.space, chosen, inv))
 
 
 def add_transform(destination: TensorMap, source: TensorMap, p, alpha=1, beta=1, *,
@@ -334,18 +425,16 @@ class ContractPlan:
     canonical: HomSpace
     gemm: stride.GemmPlan
     result: HomSpace
+    conjugate: tuple = (False, False)        # per operand, after any reversal
+    right_twist: tuple = ()                  # right canonical codomain legs to twist
 
 
 def _storage_dim(space: HomSpace) -> int:
     return degeneracy_structure(space).total_dim
 
 
-def _is_identity(space: HomSpace, p_codomain, p_domain) -> bool:
-    return tuple(p_codomain) == tuple(range(space.numout)) and tuple(p_domain) == tuple(range(space.numout, space.numind))
-
-
 def _copy_cost(space: HomSpace, p) -> int:
-    return 0 if _is_identity(space, *p) else _storage_dim(space)
+    return 0 if _is_identity_p(space, *p) else _storage_dim(space)
 
 
 def _compose_spec(left: HomSpace, right: HomSpace, result: HomSpace) -> np.ndarray:
@@ -366,31 +455,56 @@ def _compose_spec(left: HomSpace, right: HomSpace, result: HomSpace) -> np.ndarr
     return np.array(rows, np.int64).reshape(-1, 6)
 
 
+def _adjoint_axis(space: HomSpace, axis: int) -> int:
+    """A visible axis of `space` as an axis of hom(domain, codomain) (primitives.py:141-144)."""
+    return space.numin + axis if axis < space.numout else axis - space.numout
+
+
+# Families with the reference's "symmetric boson" contraction options
+# (primitives.py:399-406): reversed operand order and fused adjoint preparation.
+_SYMMETRIC_BOSONS = frozenset(("U1Irrep", "Z2Irrep", "Z3Irrep", "Z4Irrep"))
+
+
+def _symmetric_boson(space: HomSpace) -> bool:
+    return space.sector_type.name in _SYMMETRIC_BOSONS
+
+
 @lru_cache(maxsize=128)
 def contract_plan(left: HomSpace, right: HomSpace, left_axes: tuple, right_axes: tuple,
-                  output: tuple) -> ContractPlan:
+                  output: tuple, conjugate: tuple = (False, False)) -> ContractPlan:
+    """Operand permutations, sector GEMM table and result space of one
+    contraction (primitives.py:307-430); conjugated operands are seen as their
+    adjoints hom(domain, codomain)."""
     ranks = (left.numind, right.numind)
-    for la, ra in zip(left_axes, right_axes):
-        if left[la].dual() != right[ra]:
+    spaces = tuple(hom(s.domain, s.codomain) if c else s for s, c in zip((left, right), conjugate))
+
+    def mapped(operand, axis):
+        return _adjoint_axis((left, right)[operand], axis) if conjugate[operand] else axis
+
+    m_left = tuple(mapped(0, a) for a in left_axes)
+    m_right = tuple(mapped(1, a) for a in right_axes)
+    for la, ra in zip(m_left, m_right):
+        if spaces[0][la].dual() != spaces[1][ra]:
             raise ValueError("contracted axes must be dual-compatible")
     open_left = tuple(a for a in range(ranks[0]) if a not in left_axes)
     open_right = tuple(a for a in range(ranks[1]) if a not in right_axes)
+    m_open_left = tuple(mapped(0, a) for a in open_left)
+    m_open_right = tuple(mapped(1, a) for a in open_right)
     canonical_refs = tuple((0, a) for a in open_left) + tuple((1, a) for a in open_right)
     position = {ref: i for i, ref in enumerate(canonical_refs)}
     output_p = (tuple(position[r] for r in output[0]), tuple(position[r] for r in output[1]))
-    spaces = (left, right)
-    symmetric_boson = left.sector_type.bosonic
+    symmetric_boson = _symmetric_boson(spaces[0])
 
     def candidate(sort_position, reversed_operands):
-        pairs = sorted(zip(left_axes, right_axes), key=lambda pair: pair[sort_position])
+        pairs = sorted(zip(m_left, m_right), key=lambda pair: pair[sort_position])
         lc, rc = tuple(p[0] for p in pairs), tuple(p[1] for p in pairs)
         if reversed_operands:
-            lp, rp = (open_right, rc), (lc, open_left)
+            lp, rp = (m_open_right, rc), (lc, m_open_left)
             ls, rs = spaces[1], spaces[0]
-            nl, nr = len(open_left), len(open_right)
+            nl, nr = len(m_open_left), len(m_open_right)
             op = tuple(tuple(a + nr if a < nl else a - nl for a in part) for part in output_p)
         else:
-            lp, rp = (open_left, lc), (rc, open_right)
+            lp, rp = (m_open_left, lc), (rc, m_open_right)
             ls, rs = spaces
             op = output_p
         cost = _copy_cost(ls, lp) + _copy_cost(rs, rp)
@@ -404,18 +518,38 @@ def contract_plan(left: HomSpace, right: HomSpace, left_axes: tuple, right_axes:
     lspace, rspace = ls.permute(*lp), rs.permute(*rp)
     spec = _compose_spec(lspace, rspace, canonical)
     result = canonical.permute(*op)
-    return ContractPlan(lp, rp, op, rev, canonical, stride.GemmPlan(spec), result)
+    flags = tuple(conjugate[::-1]) if rev else tuple(conjugate)
+    right_twist = tuple(a for a in range(len(rp[0])) if rspace[a].is_dual) if not rspace.sector_type.bosonic else ()
+    return ContractPlan(lp, rp, op, rev, canonical, stride.GemmPlan(spec), result, flags, right_twist)
 
 
-def tensorcontract(left: TensorMap, right: TensorMap, *, axes, output) -> TensorMap:
-    """tensorcontract(A, B, axes=((2,), (0,)), output=(((0, 0), (1, 1)), ((0, 1),)))."""
+def _prepare_operand(value: TensorMap, permutation: tuple, conjugate: bool) -> TensorMap:
+    """The canonical operand (primitives.py:288-304): a permute, or for a
+    conjugated operand the permuted adjoint, computed in one conjugating pass
+    into the adjoint destination (exact, so equal to the reference's
+    adjoint-then-permute for the families without its fused path)."""
+    if not conjugate:
+        return permute(value, permutation)
+    adjoint_space = hom(value.space.domain, value.space.codomain)
+    parent = (tuple(_adjoint_axis(adjoint_space, a) for a in permutation[1]),
+              tuple(_adjoint_axis(adjoint_space, a) for a in permutation[0]))
+    return permute_adjoint(value, parent)
+
+
+def tensorcontract(left: TensorMap, right: TensorMap, *, axes, output,
+                   conjugate: tuple[bool, bool] = (False, False)) -> TensorMap:
+    """tensorcontract(A, B, axes=((2,), (0,)), output=(((0, 0), (1, 1)), ((0, 1),)),
+    conjugate=(False, True)) (primitives.py:307-430)."""
     left_axes, right_axes = tuple(int(a) for a in axes[0]), tuple(int(a) for a in axes[1])
     output = (tuple((int(o), int(a)) for o, a in output[0]), tuple((int(o), int(a)) for o, a in output[1]))
-    plan = contract_plan(left.space, right.space, left_axes, right_axes, output)
+    flags = (bool(conjugate[0]), bool(conjugate[1]))
+    plan = contract_plan(left.space, right.space, left_axes, right_axes, output, flags)
     if plan.reversed_operands:
         left, right = right, left
-    lcan = permute(left, plan.left_p)
-    rcan = permute(right, plan.right_p)
+    lcan = _prepare_operand(left, plan.left_p, plan.conjugate[0])
+    rcan = _prepare_operand(right, plan.right_p, plan.conjugate[1])
+    if plan.right_twist:
+        rcan = twist(rcan, plan.right_twist)
     dtype = torch.promote_types(lcan.data.dtype, rcan.data.dtype)
     out = torch.empty(_storage_dim(plan.canonical), dtype=dtype, device=lcan.data.device)
     stride.sector_gemm(plan.gemm, lcan.data.to(dtype).contiguous(), rcan.data.to(dtype).contiguous(), out)

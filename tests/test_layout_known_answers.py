@@ -89,3 +89,75 @@ def test_benchmark_space_sizes():
     w = space(U1Irrep, degs)
     ds = degeneracy_structure(hom((w, w), (w, w)))
     assert (ds.total_dim, len(ds.block_start), len(ds.offsets)) == (1023777634, 17, 489)
+
+
+# ---------------------------------------------------------------------------
+# Fermionic coefficients, twists, flips and traces
+# (crates/tensor0-core/tests/transform.rs).
+
+from tensor0_b200.structure import (FermionParity, flip_transform, trace_transformer, tree_permuter,  # noqa: E402
+                                    twist_factors)
+
+
+def fp(values):
+    return space(FermionParity, values)
+
+
+def test_fermion_parity_braid_coefficients():
+    # transform.rs:432-484
+    odd2, odd3, odd5, odd7 = fp({1: 2}), fp({1: 3}), fp({1: 5}), fp({1: 7})
+    even = fp({0: 1})
+    _, t = tree_permuter(hom((odd2, odd3), ()), (1, 0), ())
+    assert t.coeff.tolist() == [-1.0]
+    _, t = tree_permuter(hom((even, fp({1: 1})), (fp({1: 1}),)), (1, 0), (2,))
+    assert t.coeff.tolist() == [1.0]
+    number = ProductSector(U1Irrep, FermionParity)
+    left, right = space(number, {(0.5, 1): 1}), space(number, {(-0.5, 1): 1})
+    _, t = tree_permuter(hom((left, right), ()), (1, 0), ())
+    assert t.coeff.tolist() == [-1.0]
+    _, t = tree_permuter(hom((odd2,), (odd3,)), (1,), (0,))
+    assert t.coeff.tolist() == [-1.0]
+    _, t = tree_permuter(hom((odd2, odd3, odd5, odd7), ()), (1, 2, 0, 3), ())
+    assert t.coeff.tolist() == [1.0]
+
+
+def test_twist_factors_follow_pair_order():
+    # transform.rs:835-871
+    v = fp({0: 1, 1: 1})
+    h = hom((v,), (v,))
+    assert twist_factors(h, (0,)).tolist() == [1.0, -1.0]
+    assert twist_factors(h, (1,)).tolist() == [1.0, -1.0]
+    assert twist_factors(h, (0, 1)) is None
+    assert twist_factors(h, (0,), inv=True).tolist() == [1.0, -1.0]
+    odd, even = fp({1: 1}), fp({0: 1})
+    h = hom((odd, odd), (even, even))
+    assert twist_factors(h, (0,)).tolist() == [-1.0]
+    assert twist_factors(h, (2,)) is None
+    u = space(U1Irrep, {0: 1, 0.5: 1})
+    assert twist_factors(hom((u,), (u,)), (0,)) is None
+
+
+def test_flip_entries():
+    # transform.rs:904-930, 961-970
+    f = space(U1Irrep, {-0.5: 2, 0: 3, 0.5: 5})
+    _, t = flip_transform(hom((f,), (f,)), (0, 1))
+    assert t.coeff.tolist() == [1.0] * len(t.coeff) and t.dst.tolist() == list(range(len(t.dst)))
+    g = space(U1Irrep, {-0.5: 1, 0.5: 1})
+    _, t = flip_transform(hom((g, g), ()), (1,))
+    assert list(zip(t.dst.tolist(), t.coeff.tolist())) == [(1, 1.0), (0, 1.0)]
+    number = ProductSector(U1Irrep, FermionParity)
+    odd = space(number, {(0.5, 1): 1})
+    h = hom((odd,), (odd,))
+    assert flip_transform(h, (0,))[1].coeff.tolist() == [1.0]
+    assert flip_transform(h, (1,))[1].coeff.tolist() == [-1.0]
+
+
+def test_fermion_trace_twists_only_nondual_tail_sectors():
+    # transform.rs:723-740
+    for dual, expected in ((False, -1.0), (True, 1.0)):
+        odd = fp({1: 1}) if not dual else space(FermionParity, {1: 1}, dual=True)
+        src = hom((odd,), (odd,))
+        dst = hom((), ())
+        canonical, basis = tree_permuter(src, (0,), (1,))
+        t = trace_transformer(canonical, dst, basis)
+        assert t.coeff.tolist() == [expected]
