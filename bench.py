@@ -10,9 +10,13 @@ data from a seed:
 Algorithmic bytes per step: 2 N s + 3 N s (s = element size).  Inputs (4 GB
 for f32) exceed the 126 MB L2, so no flush is needed between steps.
 
-Multi-GPU: one process per GPU; the storage batch axis is partitioned (rank r
-owns batch element r, the reference's own data-parallel axis), so per-GPU work
-is fixed as N grows (weak scaling) and the data path has no collective.
+Multi-GPU (torchrun, one process per GPU): ONE tensor is split by sector.
+The permute's 489 records are partitioned by longest-processing-time over the
+ranks (cost = bytes moved); each rank holds its records' source sub-blocks
+compacted in its own HBM and writes their destination sub-blocks compacted,
+so the timed kernels need no communication (strong scaling: total work is
+fixed as N grows).  The NCCL all-gather of the compacted outputs plus the
+engine copy that unpacks them into the packed layout is timed separately.
 
 ``--impl reference`` times the reference's own CPU executors (oracle/_ref,
 compiled from the reference sources) on the host cores.
@@ -66,7 +70,7 @@ def workload_config(args, elements: int):
     return {"workload": "u1-4leg permute((2,0),(3,1)) + beta=1 accumulate",
             "legs": f"U1 q=-4..4, deg round({args.scale} exp(-q^2/8))", "elements": elements,
             "sub_blocks": 489, "dtype": args.dtype, "l2": "inputs larger than the 126 MB L2, no flush",
-            "parallelism": f"dp{args.gpus} over storage batch"}
+            "parallelism": "single GPU"}
 
 
 # ---------------------------------------------------------------------------
@@ -124,7 +128,7 @@ def run_reference(args, rank: int):
     threads = os.cpu_count() or 1
     value, ms, sample, n = cpu_reference_steps(args.dtype, args.steps, args.warmup, threads, args.scale)
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": args.dtype, "data": "synthetic N(0,1), seeded",
             "config": workload_config(args, n), "impl": "reference",
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "reference",
@@ -295,6 +299,165 @@ def load_traffic():
     return None
 
 
+def timed_events(stream, count, body):
+    """Device time (ms) of `count` calls of body() on `stream`, and per-call marks."""
+    import torch
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(count + 1)]
+    torch.cuda.synchronize()
+    for k in range(count):
+        marks[k].record(stream)
+        body(k)
+    marks[count].record(stream)
+    torch.cuda.synchronize()
+    return marks[0].elapsed_time(marks[count]), [marks[k].elapsed_time(marks[k + 1]) for k in range(count)]
+
+
+def max_over_ranks(value: float, device) -> float:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_sharded(args, world: int, rank: int, device):
+    """The workload split by sector over `world` ranks (see the module docstring)."""
+    import torch
+    import torch.distributed as dist
+
+    from tensor0_b200 import _native, stride
+    from tensor0_b200.sharding import gather_words, shard_capacity, shard_permute
+
+    h, _ = workload_space(args.scale)
+    plan = permute_plan_of(h)
+    item = 4 if args.dtype == "f32" else 8
+    tdtype = torch.float32 if args.dtype == "f32" else torch.complex64
+    n = plan.source_size
+    shard = shard_permute(plan, rank, world, item)
+    records = shard.records.size
+    acc = stride.Plan(_native.OP_ACCUMULATION, shard.words, element_bytes=item,
+                      coefficient_records=np.arange(records), outputs_disjoint=True)
+    upd = stride.Plan(_native.OP_UPDATE, shard.words, element_bytes=item)
+    capacity = shard_capacity(plan, world, item)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    x = torch.randn(shard.local_source_size, generator=gen, device=device, dtype=tdtype)
+    z = torch.randn(shard.local_output_size, generator=gen, device=device, dtype=tdtype)
+    y_pad = torch.zeros(capacity, device=device, dtype=tdtype)
+    y = y_pad[: shard.local_output_size]
+    ones = torch.ones(records, dtype=torch.float32, device=device)
+    alpha = torch.ones(1, dtype=torch.float32, device=device)
+    beta = torch.ones(1, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        stride.execute_accumulation(x, acc, ones, out=y)
+        stride.execute_update(x, z, alpha, beta, upd, out=z)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    launches0 = stride.kernel_launches()
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
+    with ClockSampler(device_uuid(device.index)) as clocks:
+        torch.cuda.synchronize()
+        for k in range(args.steps):
+            marks[2 * k].record(stream)
+            stride.execute_accumulation(x, acc, ones, out=y)
+            marks[2 * k + 1].record(stream)
+            stride.execute_update(x, z, alpha, beta, upd, out=z)
+        marks[2 * args.steps].record(stream)
+        torch.cuda.synchronize()
+    launches = stride.kernel_launches() - launches0
+    local_ms = marks[0].elapsed_time(marks[2 * args.steps])
+    elapsed = max_over_ranks(local_ms, device)
+    step_bytes = 5 * n * item
+    value = step_bytes * args.steps / (elapsed / 1e3) / 1e9
+    update_ms = statistics.mean(marks[2 * k + 1].elapsed_time(marks[2 * k + 2]) for k in range(args.steps))
+    permute_ms = statistics.mean(marks[2 * k].elapsed_time(marks[2 * k + 1]) for k in range(args.steps))
+    local_update_bytes = 3 * shard.local_output_size * item
+    local_permute_bytes = 2 * shard.local_output_size * item
+
+    # Gather: NCCL all-gather of the padded compacted outputs, then one engine
+    # copy unpacking them into the packed layout of the whole tensor.
+    unpack = stride.Plan(_native.OP_COPY, gather_words(plan, world, item), element_bytes=item)
+    gathered = torch.empty(world * capacity, device=device, dtype=tdtype)
+    full = torch.empty(plan.output_size, device=device, dtype=tdtype)
+
+    def gather(_=None):
+        dist.all_gather_into_tensor(gathered, y_pad)
+        stride.execute_copy(gathered, unpack, out=full)
+
+    gather()
+    torch.cuda.synchronize()
+    dist.barrier()
+    gather_steps = max(2, min(args.steps, 5))
+    gather_total, _ = timed_events(stream, gather_steps, gather)
+    gather_ms = max_over_ranks(gather_total / gather_steps, device)
+    received = (world - 1) * capacity * item
+
+    # End to end through the stride API with host buffers: each rank copies its
+    # compacted inputs in from pinned memory and its outputs back, every step.
+    e2e_steps = args.e2e_steps or min(args.steps, 8)
+    x_host = x.cpu().pin_memory()
+    z_host = z.cpu().pin_memory()
+    y_back = torch.empty(shard.local_output_size, dtype=tdtype).pin_memory()
+    z_back = torch.empty(shard.local_output_size, dtype=tdtype).pin_memory()
+    xd, zd, yd = torch.empty_like(x), torch.empty_like(z), torch.empty_like(y)
+    torch.cuda.synchronize()
+    dist.barrier()
+
+    def e2e(_):
+        xd.copy_(x_host, non_blocking=True)
+        zd.copy_(z_host, non_blocking=True)
+        stride.execute_accumulation(xd, acc, ones, out=yd)
+        stride.execute_update(xd, zd, alpha, beta, upd, out=zd)
+        y_back.copy_(yd, non_blocking=True)
+        z_back.copy_(zd, non_blocking=True)
+
+    e2e_total, _ = timed_events(stream, e2e_steps, e2e)
+    e2e_ms = max_over_ranks(e2e_total, device)
+    e2e_value = step_bytes * e2e_steps / (e2e_ms / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    if rank == 0:
+        achieved = local_update_bytes / (update_ms / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": args.dtype,
+            "data": "synthetic N(0,1) from seed (no dataset)",
+            "config": {**workload_config(args, n), "parallelism": f"sector-sharded over {world} ranks, LPT by bytes, "
+                       "compacted shards, no collective in the timed kernels"},
+            "roofline": {"bound": "hbm", "kernel": "MapKernel<update> on rank 0's shard",
+                         "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "algorithmic_bytes_per_launch": local_update_bytes,
+                         "permute_launch": {"achieved": round(local_permute_bytes / (permute_ms / 1e3) / 1e9, 2),
+                                            "frac": round(local_permute_bytes / (permute_ms / 1e3) / 1e9 / peak, 4),
+                                            "algorithmic_bytes_per_launch": local_permute_bytes}},
+            "shards": {"records_rank0": int(records), "elements_rank0": int(shard.local_output_size),
+                       "capacity": int(capacity), "elements_total": int(n)},
+            "gather": {"what": "NCCL all_gather_into_tensor of padded compacted outputs + engine copy into the "
+                               "packed layout, per rank, max over ranks",
+                       "ms": round(gather_ms, 4), "received_bytes_per_rank": int(received),
+                       "nvlink_gbs_per_rank": round(received / (gather_ms / 1e3) / 1e9, 2)},
+            "cpu_baseline": None,
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "steps": e2e_steps,
+                    "h2d_bytes_per_step": 2 * n * item, "d2h_bytes_per_step": 2 * n * item,
+                    "note": "all ranks together; each rank copies its compacted shard"},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+            "contraction": None,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def permute_plan_of(h):
+    from tensor0_b200.tensor_map import permute_plan
+    return permute_plan(h, (2, 0), (3, 1))
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -315,6 +478,12 @@ def main():
     device = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+        try:
+            run_sharded(args, world, rank, device)
+        finally:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
 
     h, _ = workload_space(args.scale)
     plan = permute_plan(h, (2, 0), (3, 1))
@@ -324,9 +493,9 @@ def main():
     acc_plan = plan.engine_plan(_native.OP_ACCUMULATION, tdtype)
     upd_plan = plan.engine_plan(_native.OP_UPDATE, tdtype)
 
-    # Synthetic N(0, 1) storage for this rank's batch element.
+    # Synthetic N(0, 1) storage.
     gen = torch.Generator(device=device)
-    gen.manual_seed(1000 + rank)
+    gen.manual_seed(1000)
     x = torch.randn(n, generator=gen, device=device, dtype=tdtype)
     z = torch.randn(n, generator=gen, device=device, dtype=tdtype)
     y = torch.empty_like(x)
@@ -341,8 +510,6 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
 
     stream = torch.cuda.current_stream(device)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
@@ -364,12 +531,8 @@ def main():
     elapsed = start.elapsed_time(end)
     permute_ms = [marks[2 * k].elapsed_time(marks[2 * k + 1]) for k in range(args.steps)]
     update_ms = [marks[2 * k + 1].elapsed_time(marks[2 * k + 2]) for k in range(args.steps)]
-    if world > 1:
-        t = torch.tensor([elapsed], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
     step_bytes = 5 * n * item
-    value = world * step_bytes * args.steps / (elapsed / 1e3) / 1e9
+    value = step_bytes * args.steps / (elapsed / 1e3) / 1e9
 
     peak, peak_kind = load_peaks()
     update_bytes = 3 * n * item
@@ -397,8 +560,6 @@ def main():
     computed = [torch.cuda.Event() for _ in range(2)]
     drained = [torch.cuda.Event() for _ in range(2)]
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
     e_start.record(h2d)
@@ -424,46 +585,38 @@ def main():
     e_end.record(d2h)
     torch.cuda.synchronize()
     e_elapsed = e_start.elapsed_time(e_end)
-    if world > 1:
-        t = torch.tensor([e_elapsed], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_elapsed = float(t.item())
-    e2e_value = world * step_bytes * e2e_steps / (e_elapsed / 1e3) / 1e9
+    e2e_value = step_bytes * e2e_steps / (e_elapsed / 1e3) / 1e9
 
     contraction = None
-    if rank == 0 and not args.no_contraction:
+    if not args.no_contraction:
         contraction = contraction_bench(device, max(args.steps, 5), args.warmup)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         value_cpu, ms_cpu, sample, _ = cpu_reference_steps(args.dtype, 3, 1, threads, SAMPLE_SCALE)
         cpu = {"value": round(value_cpu, 3), "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample}
 
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
-            "data": "synthetic N(0,1) from seed (no dataset)", "config": workload_config(args, n),
-            "roofline": {"bound": "hbm", "kernel": "MapKernel<update> (beta=1 accumulate launch)",
-                         "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": load_traffic(),
-                         "algorithmic_bytes_per_launch": update_bytes,
-                         "permute_launch": {"achieved": round(permute_achieved, 2),
-                                            "frac": round(permute_achieved / peak, 4),
-                                            "algorithmic_bytes_per_launch": permute_bytes}},
-            "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "steps": e2e_steps,
-                    "h2d_bytes_per_step": 2 * n * item, "d2h_bytes_per_step": 2 * n * item},
-            "gpu_launches": int(launches),
-            "clocks": clocks.summary(),
-            "contraction": contraction,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": args.dtype,
+        "data": "synthetic N(0,1) from seed (no dataset)", "config": workload_config(args, n),
+        "roofline": {"bound": "hbm", "kernel": "MapKernel<update> (beta=1 accumulate launch)",
+                     "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": load_traffic(),
+                     "algorithmic_bytes_per_launch": update_bytes,
+                     "permute_launch": {"achieved": round(permute_achieved, 2),
+                                        "frac": round(permute_achieved / peak, 4),
+                                        "algorithmic_bytes_per_launch": permute_bytes}},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "steps": e2e_steps,
+                "h2d_bytes_per_step": 2 * n * item, "d2h_bytes_per_step": 2 * n * item},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+        "contraction": contraction,
+    }
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

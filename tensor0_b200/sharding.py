@@ -110,3 +110,52 @@ def shard_permute(plan, rank: int, world: int, element_bytes: int = 8) -> Permut
     return PermuteShard(rank, world, owned, src_sizes, src_strides, sd.offsets[src_idx], dst_sizes,
                         plan.dst_strides[owned], plan.dst_offsets[owned], local_offsets, local_offsets, total, total,
                         words)
+
+
+def shard_capacity(plan, world: int, element_bytes: int = 8) -> int:
+    """Largest local output (elements) over the shards: the padded size of
+    one rank's part of an all-gather."""
+    return max(shard_permute(plan, r, world, element_bytes).local_output_size for r in range(world))
+
+
+def gather_words(plan, world: int, element_bytes: int = 8) -> np.ndarray:
+    """Copy layout words that unpack an all-gathered buffer — shard r's
+    compacted destination sub-blocks at r * capacity — into the packed
+    destination layout of the whole tensor (one engine copy)."""
+    from .structure import degeneracy_structure
+
+    capacity = shard_capacity(plan, world, element_bytes)
+    shapes, src_strides, src_offsets, dst_strides, dst_offsets = [], [], [], [], []
+    for r in range(world):
+        shard = shard_permute(plan, r, world, element_bytes)
+        if not shard.records.size:
+            continue
+        shapes.append(shard.dst_sizes)
+        src_strides.append(_row_major(shard.dst_sizes))
+        src_offsets.append(r * capacity + shard.local_dst_offsets)
+        dst_strides.append(shard.dst_strides)
+        dst_offsets.append(shard.dst_offsets)
+    return stride.encode_layout_arrays(np.concatenate(shapes), np.concatenate(src_strides),
+                                       np.concatenate(src_offsets), np.concatenate(dst_strides),
+                                       np.concatenate(dst_offsets), source_size=world * capacity,
+                                       output_size=degeneracy_structure(plan.dst).total_dim)
+
+
+def scatter_words(plan, rank: int, world: int, element_bytes: int = 8, *, source: bool = True) -> np.ndarray:
+    """Copy layout words that extract shard `rank`'s sub-blocks from the packed
+    layout of the whole tensor into its compacted local buffer: the source
+    sub-blocks (`source`, for distributing inputs) or the destination
+    sub-blocks (for a shard's share of an existing output)."""
+    shard = shard_permute(plan, rank, world, element_bytes)
+    from .structure import degeneracy_structure
+
+    if source:
+        sizes, strides, offsets = shard.src_sizes, shard.src_strides, shard.src_offsets
+        local, total = shard.local_src_offsets, shard.local_source_size
+        whole = degeneracy_structure(plan.src).total_dim
+    else:
+        sizes, strides, offsets = shard.dst_sizes, shard.dst_strides, shard.dst_offsets
+        local, total = shard.local_dst_offsets, shard.local_output_size
+        whole = degeneracy_structure(plan.dst).total_dim
+    compact = _row_major(sizes) if len(sizes) else np.zeros_like(sizes)
+    return stride.encode_layout_arrays(sizes, strides, offsets, compact, local, source_size=whole, output_size=total)

@@ -242,3 +242,38 @@ def test_wide_offset_kernels_bit_exact(dtype):
     update = stride.Plan(_native.OP_UPDATE, words, element_bytes=eb, wide_offsets=True)
     got = host(stride.execute_update(torch.from_numpy(x).cuda(), torch.from_numpy(base).cuda(), 1.0, 0.5, update))
     assert np.array_equal(bits(got), bits(so.update(words, x, base, real(1.0), real(0.5))))
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_sector_shards_gathered_equal_the_single_launch(world):
+    """The multi-GPU split run on one GPU: each LPT shard's compacted source is
+    scattered out of the packed tensor, permuted and accumulated by its own
+    plans, the padded outputs are concatenated as an all-gather would and one
+    engine copy unpacks them; the result equals the single launch bit for bit."""
+    from tensor0_b200.sharding import gather_words, scatter_words, shard_capacity, shard_permute
+    h = four_leg_space(24)
+    plan = permute_plan(h, (2, 0), (3, 1))
+    x = device_normal(plan.source_size, np.float32, 31)
+    base = device_normal(plan.output_size, np.float32, 32)
+    y = permute(TensorMap(h, x), ((2, 0), (3, 1)))
+    z = add_transform(TensorMap(y.space, base.clone()), TensorMap(h, x), ((2, 0), (3, 1)), 1.0, 1.0)
+    capacity = shard_capacity(plan, world, 4)
+    gathered_y = torch.zeros(world * capacity, device="cuda")
+    gathered_z = torch.zeros(world * capacity, device="cuda")
+    one = torch.ones(1, device="cuda")
+    for r in range(world):
+        shard = shard_permute(plan, r, world, 4)
+        scatter_x = stride.Plan(_native.OP_COPY, scatter_words(plan, r, world, 4), element_bytes=4)
+        scatter_b = stride.Plan(_native.OP_COPY, scatter_words(plan, r, world, 4, source=False), element_bytes=4)
+        xl = stride.execute_copy(x, scatter_x)
+        bl = stride.execute_copy(base, scatter_b)
+        acc = stride.Plan(_native.OP_ACCUMULATION, shard.words, element_bytes=4,
+                          coefficient_records=np.arange(shard.records.size), outputs_disjoint=True)
+        upd = stride.Plan(_native.OP_UPDATE, shard.words, element_bytes=4)
+        stride.execute_accumulation(xl, acc, torch.ones(shard.records.size, device="cuda"),
+                                    out=gathered_y[r * capacity: r * capacity + shard.local_output_size])
+        stride.execute_update(xl, bl, one, one, upd, out=gathered_z[r * capacity: r * capacity + shard.local_output_size])
+    unpack = stride.Plan(_native.OP_COPY, gather_words(plan, world, 4), element_bytes=4)
+    torch.cuda.synchronize()
+    assert torch.equal(stride.execute_copy(gathered_y, unpack).view(torch.int32), y.data.view(torch.int32))
+    assert torch.equal(stride.execute_copy(gathered_z, unpack).view(torch.int32), z.data.view(torch.int32))
