@@ -46,6 +46,7 @@ extern "C" {
 /* Plan operations (the reference's operation codes, descriptor.h:69-78). */
 #define T0B_OP_COPY 0
 #define T0B_OP_UPDATE 1
+#define T0B_OP_DOT 2
 #define T0B_OP_ACCUMULATION 3
 #define T0B_OP_REDUCTION 4
 
@@ -73,7 +74,9 @@ const char* t0b_version(void);
 
 /*
  * Build a plan from layout words.
- *   operation: T0B_OP_COPY / UPDATE / ACCUMULATION take i64 words (v1);
+ *   operation: T0B_OP_COPY / UPDATE / DOT / ACCUMULATION take i64 words (v1;
+ *              for DOT the record's source side addresses the left operand
+ *              and its destination side the right one, both only bounds-checked);
  *              T0B_OP_REDUCTION takes the reduction protocol's u64 words
  *              (little-endian bit patterns carried as i64), as the reference's
  *              Tensor0StridePrepareLayout bridge does (descriptor.cc:321-340).
@@ -191,6 +194,20 @@ int t0b_update(const t0b_plan* plan, int32_t dtype, const void* source, const vo
                void* output, int64_t batches, const void* alpha, int32_t alpha_dtype,
                int64_t alpha_count, const void* beta, int32_t beta_dtype, int64_t beta_count,
                const int64_t* device_table, void* stream, char* error, size_t error_size);
+
+/*
+ * Dot (the reference's dot_p): out[b] = sum over every record and element of
+ * conj?(left[b, src(i)]) * right[b, dst(i)], conjugating the left factor when
+ * conjugate_left is 1 (complex storage).  left [batches, source_size], right
+ * [batches, output_size], output [batches].  scratch: batches *
+ * t0b_plan_scratch_elements() elements of the storage type for the partial
+ * sums (XLA-owned in the reference, dot.cu:123-160), 16-byte aligned.  At most
+ * 65535 batches.
+ * Replaces Tensor0StrideCudaDot{F32,F64,C64,C128}V1 (dot.cu:97-160).
+ */
+int t0b_dot(const t0b_plan* plan, int32_t dtype, const void* left, const void* right, void* output,
+            int64_t batches, int32_t conjugate_left, void* scratch, const int64_t* device_table,
+            void* stream, char* error, size_t error_size);
 
 /*
  * TensorMap.add: out[i] = alpha * x[i] + beta * y[i] over n elements, with

@@ -144,6 +144,19 @@ def reduction(words, source: np.ndarray, output_size: int, coefficients=(), coef
     return out
 
 
+def dot(words, left: np.ndarray, right: np.ndarray, conjugate_left: bool = False, threads: int = 1) -> np.ndarray:
+    left = np.ascontiguousarray(left)
+    right = np.ascontiguousarray(right)
+    batches = int(np.prod(left.shape[:-1], dtype=np.int64))
+    out = np.full(left.shape[:-1], 7, dtype=left.dtype)
+    words = _words(words)
+    _call(lib().t0ref_dot, ctypes.c_int(_DTYPES[left.dtype]), words.ctypes.data_as(c_i64p),
+          ctypes.c_size_t(words.size), ctypes.c_int64(int(conjugate_left)), ctypes.c_void_p(left.ctypes.data),
+          ctypes.c_int64(left.shape[-1]), ctypes.c_void_p(right.ctypes.data), ctypes.c_int64(right.shape[-1]),
+          ctypes.c_void_p(out.ctypes.data), ctypes.c_int64(batches), ctypes.c_int64(threads))
+    return out
+
+
 def update(words, source: np.ndarray, base: np.ndarray, alpha, beta, threads: int = 1,
            out: np.ndarray | None = None) -> np.ndarray:
     source = np.ascontiguousarray(source)

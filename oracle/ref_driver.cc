@@ -15,6 +15,7 @@
 // timing covers execution only.
 
 #define TENSOR0_STRIDE_TEST_NO_HANDLERS
+#include "ffi/dot_impl.h"
 #include "ffi/reduction_impl.h"
 #include "ffi/update_impl.h"
 #include "execute/copy.h"
@@ -300,6 +301,26 @@ int t0ref_update(int dtype, const int64_t* words, size_t word_count,
     auto future = native::Update<Dtype>({words, word_count}, prepared->get(), ffi::AnyBuffer(&input),
         ffi::BufferR2<Dtype>(&old), ffi::AnyBuffer(&a), ffi::AnyBuffer(&b),
         ffi::BufferR2<Dtype>(&result), Pool(threads).Get());
+    return Wait(std::move(future), error, error_size);
+  });
+}
+
+// Dot: InstantiateDot (prepared.cc:66-75) + Dot (ffi/dot_impl.h:51-110).
+int t0ref_dot(int dtype, const int64_t* words, size_t word_count, int64_t conjugate_left, const void* left,
+              int64_t left_size, const void* right, int64_t right_size, void* output, int64_t batches,
+              int64_t threads, char* error, size_t error_size) {
+  auto prepared = native::InstantiateDot({words, word_count}, conjugate_left);
+  if (!prepared.has_value()) return Report(prepared.error(), error, error_size);
+  return DispatchStorage(dtype, [&](auto tag) {
+    constexpr auto Dtype = decltype(tag)::value;
+    int64_t left_dims[2] = {batches, left_size};
+    int64_t right_dims[2] = {batches, right_size};
+    int64_t output_dims[1] = {batches};
+    auto a = MakeBuffer(dtype, left, 2, left_dims);
+    auto b = MakeBuffer(dtype, right, 2, right_dims);
+    auto result = MakeBuffer(dtype, output, 1, output_dims);
+    auto future = native::Dot<Dtype>({words, word_count}, conjugate_left, prepared->get(), ffi::AnyBuffer(&a),
+                                     ffi::AnyBuffer(&b), ffi::BufferR1<Dtype>(&result), Pool(threads).Get());
     return Wait(std::move(future), error, error_size);
   });
 }

@@ -221,3 +221,18 @@ def sector_gemm(spec, left: np.ndarray, right: np.ndarray, output_size: int) -> 
         B = right[b:b + k * n].reshape(k, n).astype(wide)
         out[c:c + m * n] = (A @ B).reshape(-1)
     return out
+
+
+def dot(words, left: np.ndarray, right: np.ndarray, conjugate_left: bool = False) -> np.ndarray:
+    """Dot: sum over records and elements of conj?(left[src]) * right[dst],
+    per batch (execute/dot.h:21-56; map_reduce_policies.cuh:103-121)."""
+    _, _, records = decode_layout(words)
+    wide = np.complex128 if np.iscomplexobj(left) else np.float64
+    out = np.zeros(left.shape[:-1], wide)
+    for shape, sstr, so, dstr, do in records:
+        if int(np.prod(shape)) == 0:
+            continue
+        a = left[..., addresses(shape, sstr, so)].astype(wide)
+        b = right[..., addresses(shape, dstr, do)].astype(wide)
+        out = out + np.sum((np.conj(a) if conjugate_left else a) * b, axis=-1)
+    return out

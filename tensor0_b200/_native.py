@@ -14,7 +14,7 @@ from . import build as _build
 LIBRARY_PATH = _build.LIBRARY
 
 S32, F32, F64, C64, C128 = 4, 11, 12, 15, 18
-OP_COPY, OP_UPDATE, OP_ACCUMULATION, OP_REDUCTION = 0, 1, 3, 4
+OP_COPY, OP_UPDATE, OP_DOT, OP_ACCUMULATION, OP_REDUCTION = 0, 1, 2, 3, 4
 PLAN_OUTPUTS_DISJOINT = 1
 PLAN_WIDE_OFFSETS = 2
 PLAN_CONJUGATE_SOURCE = 4
@@ -63,6 +63,9 @@ SIGNATURES = {
                                   ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
                                   ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
                                   ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "t0b_dot": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                               ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                               ctypes.c_char_p, ctypes.c_size_t]),
     "t0b_axpby": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64, ctypes.c_double, ctypes.c_double,
                                  ctypes.c_void_p, ctypes.c_double, ctypes.c_double, ctypes.c_void_p,
                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),

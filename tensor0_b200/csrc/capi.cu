@@ -273,7 +273,7 @@ void t0b_plan_query(const t0b_plan* plan, t0b_plan_info* info) {
   info->output_size = p.output_size;
   info->records = p.records;
   info->tiles = p.map_tiles;
-  info->kernels_per_call = (p.has_map ? 1 : 0) + 2 * p.waves.size();
+  info->kernels_per_call = p.operation == 2 ? 2 : (p.has_map ? 1 : 0) + 2 * p.waves.size();
   info->full_coverage = p.full_coverage ? 1 : 0;
   info->bytes_moved = p.bytes_moved;
 }
@@ -371,6 +371,53 @@ int t0b_update(const t0b_plan* plan, int32_t dtype, const void* source, const vo
       RunMap(plan, t0b::kOpUpdate, dtype, alpha_dtype, beta_dtype, source, base, output, batches, alpha,
              static_cast<int64_t>(a_count), beta, static_cast<int64_t>(b_count), device_table, s);
     }
+  });
+}
+
+int t0b_dot(const t0b_plan* plan, int32_t dtype, const void* left, const void* right, void* output,
+            int64_t batches, int32_t conjugate_left, void* scratch, const int64_t* device_table, void* stream,
+            char* error, size_t error_size) {
+  return Guard(error, error_size, [&] {
+    RequirePlan(plan, 2, dtype, batches);
+    if (conjugate_left != 0 && conjugate_left != 1) throw t0b::InvalidArgument("dot conjugate_left must be zero or one");
+    const auto& p = plan->plan;
+    const int eb = p.element_bytes;
+    const uint64_t b = static_cast<uint64_t>(batches);
+    const uint64_t out_bytes = Bytes(b, eb);
+    const uint64_t left_bytes = Bytes(b * p.source_size, eb);
+    const uint64_t right_bytes = Bytes(b * p.output_size, eb);
+    const uint64_t scratch_bytes = Bytes(b * p.scratch, eb);
+    if (b == 0) return;
+    if (output == nullptr || scratch == nullptr) throw t0b::InvalidArgument("dot output or scratch buffer is null");
+    if ((p.source_size != 0 && left == nullptr) || (p.output_size != 0 && right == nullptr)) {
+      throw t0b::InvalidArgument("dot input buffer is null");
+    }
+    if (device_table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+    RequireTableAligned(device_table);
+    for (const void* buffer : {left, right, static_cast<const void*>(output)}) RequireAligned(buffer, eb, "dot");
+    // Single-precision partial sums are kept in double precision.
+    RequireAligned(scratch, 16, "dot scratch");
+    const size_t table_bytes = p.table.size() * sizeof(int64_t);
+    for (const auto& target : {std::pair<const void*, uint64_t>{output, out_bytes}, {scratch, scratch_bytes}}) {
+      Disjoint(left, left_bytes, target.first, target.second);
+      Disjoint(right, right_bytes, target.first, target.second);
+      Disjoint(device_table, table_bytes, target.first, target.second);
+    }
+    Disjoint(output, out_bytes, scratch, scratch_bytes);
+    const auto& h = Header(plan);
+    t0b::DotArgs args{};
+    args.recs = reinterpret_cast<const t0b::DotRecord*>(device_table + h.dot_offset);
+    args.nrec = h.dot_records;
+    args.units = h.dot_units;
+    args.batches = batches;
+    args.left = left;
+    args.right = right;
+    args.out = output;
+    args.partials = scratch;
+    args.left_size = static_cast<int64_t>(p.source_size);
+    args.right_size = static_cast<int64_t>(p.output_size);
+    args.conjugate_left = conjugate_left;
+    t0b::LaunchDot(dtype, args, static_cast<cudaStream_t>(stream));
   });
 }
 

@@ -754,6 +754,108 @@ __global__ void __launch_bounds__(kThreads) ReduceFinish(ReduceArgs args) {
 }
 
 // ---------------------------------------------------------------------------
+// Dot engine: out[b] = sum of conj?(left[src]) * right[dst] over every element
+// of every record.  Pass 1: CTA (x, b) walks a contiguous range of units of
+// batch b, one unit (a chunk of one row) per warp at a time with lanes
+// striding the chunk, and writes its sum to partials[b][x]; pass 2 sums the
+// partials of each batch in index order.  Deterministic for a given grid.
+// Products are rounded in the storage precision (as the reference's
+// arithmetic::Product); single-precision sums accumulate in double precision
+// and round once at the end, so long sums stay within the stated tolerance.
+// The partials live in the caller's scratch (kDotPartials storage elements
+// per batch), as DotSum values.
+
+template <typename T> struct DotSumOf { using type = T; };
+template <> struct DotSumOf<float> { using type = double; };
+template <> struct DotSumOf<float2> { using type = double2; };
+
+__device__ __forceinline__ double Widen(float v) { return v; }
+__device__ __forceinline__ double2 Widen(float2 v) { return {v.x, v.y}; }
+__device__ __forceinline__ double Widen(double v) { return v; }
+__device__ __forceinline__ double2 Widen(double2 v) { return v; }
+__device__ __forceinline__ float Narrow(double v, float*) { return __double2float_rn(v); }
+__device__ __forceinline__ float2 Narrow(double2 v, float2*) { return {__double2float_rn(v.x), __double2float_rn(v.y)}; }
+__device__ __forceinline__ double Narrow(double v, double*) { return v; }
+__device__ __forceinline__ double2 Narrow(double2 v, double2*) { return v; }
+
+template <typename T>
+__device__ __forceinline__ T DotProduct(T a, T b, bool conjugate) {
+  if constexpr (Elem<T>::kComplex) {
+    if (conjugate) a.y = -a.y;
+    return Scale(a, b);
+  } else {
+    return Mul(a, b);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) DotPartials(DotArgs a) {
+  using S = typename DotSumOf<T>::type;
+  const int64_t batch = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarps;
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  const int64_t per = (a.units + warps - 1) / warps;
+  const int64_t first = w * per, last = min(a.units, first + per);
+  const T* __restrict__ left = static_cast<const T*>(a.left) + batch * a.left_size;
+  const T* __restrict__ right = static_cast<const T*>(a.right) + batch * a.right_size;
+  const bool conjugate = a.conjugate_left != 0;
+  S acc{};
+  int64_t rec = 0;
+  if (first < last) {
+    int64_t lo = 0, hi = a.nrec - 1;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi + 1) >> 1;
+      if (a.recs[mid].unit_begin <= first) lo = mid; else hi = mid - 1;
+    }
+    rec = lo;
+  }
+  for (int64_t u = first; u < last; ++u) {
+    while (rec + 1 < a.nrec && a.recs[rec + 1].unit_begin <= u) ++rec;
+    const DotRecord& r = a.recs[rec];
+    uint32_t q = static_cast<uint32_t>(u - r.unit_begin);
+    const uint32_t row = Division(r.div[0]).Div(q);
+    const int chunk = static_cast<int>(q - row * static_cast<uint32_t>(r.chunks));
+    q = row;
+    int64_t lo_off = r.left_off, ro_off = r.right_off;
+    for (int ax = 1; ax < r.rank; ++ax) {
+      const uint32_t next = Division(r.div[ax]).Div(q);
+      const int64_t idx = q - next * static_cast<uint32_t>(r.n[ax]);
+      q = next;
+      lo_off += idx * r.sl[ax];
+      ro_off += idx * r.sr[ax];
+    }
+    const int begin = chunk * r.chunk;
+    const int end = min(r.n[0], begin + r.chunk);
+    const int64_t sl = r.sl[0], sr = r.sr[0];
+    for (int j = begin + lane; j < end; j += 32) {
+      acc = Add(acc, Widen(DotProduct(left[lo_off + j * sl], right[ro_off + j * sr], conjugate)));
+    }
+  }
+  acc = WarpSum(acc);
+  __shared__ S sums[kWarps];
+  if (lane == 0) sums[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    S total = sums[0];
+    for (int k = 1; k < kWarps; ++k) total = Add(total, sums[k]);
+    S* partials = reinterpret_cast<S*>(static_cast<T*>(a.partials) + batch * kDotPartials);
+    partials[blockIdx.x] = total;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32) DotFinish(DotArgs a, int parts) {
+  using S = typename DotSumOf<T>::type;
+  const int64_t batch = blockIdx.x;
+  const S* partials = reinterpret_cast<const S*>(static_cast<const T*>(a.partials) + batch * kDotPartials);
+  S acc{};
+  for (int k = threadIdx.x; k < parts; k += 32) acc = Add(acc, partials[k]);
+  acc = WarpSum(acc);
+  if (threadIdx.x == 0) static_cast<T*>(a.out)[batch] = Narrow(acc, static_cast<T*>(nullptr));
+}
+
+// ---------------------------------------------------------------------------
 // TensorMap.add.
 
 template <typename T, typename S>
@@ -914,6 +1016,26 @@ void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaS
         }
       }
     });
+  });
+}
+
+void LaunchDot(int32_t dtype, const DotArgs& args, cudaStream_t stream) {
+  if (args.batches == 0) return;
+  if (args.batches > 65535) throw InvalidArgumentError("dot supports at most 65535 batches per call");
+  const int64_t warps_wanted = std::max<int64_t>(1, args.units / 4);
+  WithStorage(dtype, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    // Partials are double precision for single-precision storage: half as many fit.
+    const int64_t fit = sizeof(typename DotSumOf<T>::type) > sizeof(T) ? kDotPartials / 2 : kDotPartials;
+    const int parts = static_cast<int>(std::min<int64_t>(
+        fit, std::min<int64_t>((warps_wanted + kWarps - 1) / kWarps,
+                               std::max<int64_t>(1, int64_t{SmCount()} * 8 / args.batches))));
+    DotPartials<T><<<dim3(static_cast<unsigned>(parts), static_cast<unsigned>(args.batches)), kThreads, 0, stream>>>(args);
+    Check(cudaGetLastError(), "dot launch");
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+    DotFinish<T><<<static_cast<unsigned>(args.batches), 32, 0, stream>>>(args, parts);
+    Check(cudaGetLastError(), "dot finish launch");
+    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   });
 }
 

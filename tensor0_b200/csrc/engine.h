@@ -53,6 +53,20 @@ struct ReduceArgs {
   int conjugate;                    // read conj(source) (complex storage)
 };
 
+struct DotArgs {
+  const DotRecord* recs;
+  int64_t nrec;
+  int64_t units;                    // per batch
+  int64_t batches;
+  const void* left;
+  const void* right;
+  void* out;                        // [batches]
+  void* partials;                   // [batches][kDotPartials]
+  int64_t left_size;
+  int64_t right_size;
+  int conjugate_left;
+};
+
 extern std::atomic<uint64_t> g_kernel_launches;
 
 // Throw std::runtime_error for a failed CUDA runtime call.
@@ -66,6 +80,7 @@ int64_t MapSharedBytes(int op, int64_t tile_elems, int element_bytes);
 void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const MapArgs& args,
                int smem, bool wide, cudaStream_t stream);
 void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream);
+void LaunchDot(int32_t dtype, const DotArgs& args, cudaStream_t stream);
 void LaunchAxpby(int32_t dtype, int64_t n, double ar, double ai, const void* x, double br, double bi,
                  const void* y, void* out, cudaStream_t stream);
 

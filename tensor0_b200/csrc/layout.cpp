@@ -169,7 +169,9 @@ Layout DecodeLayout(const int64_t* words, std::size_t word_count, Validation val
     for (auto& stride : record.dstr) stride = reader.Next(truncated);
     CheckAddressRecord(record, layout.source_size, layout.output_size);
     const uint64_t count = ElementCount(record);
-    if (validation == Validation::kMap) {
+    if (validation == Validation::kAddress) {
+      // Dot reads both sides; neither needs to be injective.
+    } else if (validation == Validation::kMap) {
       const bool has_zero = std::find(record.shape.begin(), record.shape.end(), 0) != record.shape.end();
       ProveInjective(record, false, has_zero ? std::vector<std::size_t>{} : AllAxes(rank));
     } else if (count != 0) {

@@ -40,6 +40,7 @@ struct Layout {
 enum class Validation {
   kMap,           // copy / update: injective destinations (DecodeLayout)
   kAccumulation,  // injective over nonzero destination strides (DecodeAccumulationLayout)
+  kAddress,       // dot: both sides only in bounds (DecodeAddressLayout)
 };
 
 Layout DecodeLayout(const int64_t* words, std::size_t word_count, Validation validation);

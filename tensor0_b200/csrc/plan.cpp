@@ -379,6 +379,71 @@ void Append(std::vector<int64_t>& table, const std::vector<T>& items) {
   if (words) std::memcpy(table.data() + at, items.data(), words * sizeof(int64_t));
 }
 
+// Dot: out[b] = sum over records and elements of conj?(left[src]) * right[dst]
+// (the reference's dot_p; execute/dot.h).  Records are canonicalised with
+// both sides' contiguous axes fused; the row (axis 0) is cut into units of at
+// most kDotChunk elements.
+constexpr int64_t kDotChunk = 1024;
+
+Plan BuildDotPlan(const int64_t* words, std::size_t word_count, int32_t element_bytes, uint32_t flags) {
+  Layout layout = DecodeLayout(words, word_count, Validation::kAddress);
+  Plan plan;
+  plan.operation = 2;
+  plan.element_bytes = element_bytes;
+  plan.flags = flags;
+  plan.source_size = layout.source_size;
+  plan.output_size = layout.output_size;
+  plan.records = layout.records.size();
+  std::vector<DotRecord> dots;
+  int64_t units = 0;
+  uint64_t elements = 0;
+  for (const Record& original : layout.records) {
+    if (ElementCount(original) == 0) continue;
+    Record record = original;
+    Canonicalize(record, true);
+    for (Record& piece : SplitForDevice(record)) {
+      DotRecord d{};
+      d.left_off = piece.src_off;
+      d.right_off = piece.dst_off;
+      d.unit_begin = units;
+      const int rank = static_cast<int>(piece.shape.size());
+      d.rank = std::max(rank, 1);
+      for (int a = 0; a < kMaxRank; ++a) { d.n[a] = 1; d.sl[a] = 0; d.sr[a] = 0; }
+      for (int a = 0; a < rank; ++a) {
+        d.n[a] = static_cast<int32_t>(piece.shape[a]);
+        d.sl[a] = piece.sstr[a];
+        d.sr[a] = piece.dstr[a];
+      }
+      d.chunk = static_cast<int32_t>(std::min<int64_t>(d.n[0], kDotChunk));
+      d.chunks = static_cast<int32_t>(CeilDiv(d.n[0], d.chunk));
+      int64_t record_units = d.chunks;
+      for (int a = 1; a < d.rank; ++a) record_units *= d.n[a];
+      if (units + record_units >= (int64_t{1} << 31)) {
+        throw std::runtime_error("a dot layout spans more than 2^31 work units per batch");
+      }
+      d.div[0] = MakeDivision(static_cast<uint32_t>(d.chunks));
+      for (int a = 1; a < kMaxRank; ++a) d.div[a] = MakeDivision(static_cast<uint32_t>(std::max(d.n[a], 1)));
+      units += record_units;
+      elements += ElementCount(piece);
+      dots.push_back(d);
+    }
+  }
+  plan.dot_units = static_cast<uint64_t>(units);
+  plan.scratch = kDotPartials;
+  plan.bytes_moved = 2 * elements * static_cast<uint64_t>(element_bytes);
+  TableHeader header{};
+  header.version = kTableVersion;
+  header.scratch = kDotPartials;
+  plan.table.assign(sizeof(TableHeader) / sizeof(int64_t), 0);
+  header.dot_offset = static_cast<int64_t>(plan.table.size());
+  header.dot_records = static_cast<int64_t>(dots.size());
+  header.dot_units = units;
+  Append(plan.table, dots);
+  header.map_offset = header.group_offset = header.reduce_offset = static_cast<int64_t>(plan.table.size());
+  std::memcpy(plan.table.data(), &header, sizeof(header));
+  return plan;
+}
+
 }  // namespace
 
 Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
@@ -386,6 +451,11 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
                int32_t element_bytes, uint32_t flags) {
   if (element_bytes != 4 && element_bytes != 8 && element_bytes != 16) {
     throw InvalidArgument("element size must be 4, 8 or 16 bytes");
+  }
+  if (operation == 2) {
+    if (coefficient_count != 0) throw InvalidArgument("dot plans take no coefficient records");
+    if ((flags & 4u) != 0) throw InvalidArgument("source conjugation is supported for accumulation and reduction plans");
+    return BuildDotPlan(words, word_count, element_bytes, flags);
   }
   Layout layout;
   switch (operation) {

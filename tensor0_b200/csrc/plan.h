@@ -98,6 +98,26 @@ struct alignas(16) ReduceRecord {
   int32_t fiber_count;
 };
 
+// Dot record: axis 0 (the smallest right stride after canonicalisation) is
+// the row walked by a warp in chunks of `chunk` elements; a unit is one chunk
+// of one row.
+struct alignas(16) DotRecord {
+  int64_t left_off;
+  int64_t right_off;
+  int64_t unit_begin;       // first unit of this record within one batch
+  int64_t sl[kMaxRank];     // left strides, axis 0 first
+  int64_t sr[kMaxRank];     // right strides
+  int32_t n[kMaxRank];      // extents
+  int32_t rank;
+  int32_t chunk;            // elements of a row per unit
+  int32_t chunks;           // units per row
+  int32_t pad_;
+  DivisionConstants div[kMaxRank];   // unit -> (chunk, row index): by chunks, then n[1], n[2], ...
+};
+
+// Partial sums per batch of the dot engine's first pass.
+constexpr int64_t kDotPartials = 1184;
+
 struct TableHeader {
   int64_t version;          // kTableVersion
   int64_t map_records;
@@ -110,7 +130,10 @@ struct TableHeader {
   int64_t tasks;            // pass-1 tasks per batch
   int64_t owners;           // pass-2 threads per batch
   int64_t scratch;          // scratch elements per batch
-  int64_t reserved[5];
+  int64_t dot_records;
+  int64_t dot_offset;
+  int64_t dot_units;        // units per batch
+  int64_t reserved[2];
 };
 
 constexpr int64_t kTableVersion = 0x7430620002;
@@ -139,6 +162,7 @@ struct Plan {
   uint64_t owners = 0;
   uint64_t scratch = 0;
   uint64_t bytes_moved = 0;      // algorithmic bytes of one batch
+  uint64_t dot_units = 0;        // dot plans: work units per batch
   std::vector<Wave> waves;       // reduce-engine waves, in order
   std::vector<int64_t> table;    // packed device table (host words)
 };

@@ -303,6 +303,31 @@ def execute_update(source: torch.Tensor, base: torch.Tensor, alpha, beta, plan: 
     return out
 
 
+def execute_dot(left: torch.Tensor, right: torch.Tensor, plan: Plan, *, conjugate_left: bool = False,
+                out: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """out[...] = sum of conj?(left[src]) * right[dst] over the plan's records
+    (the reference's execute_dot, _calls.py:126-153; dot.cu:97-160)."""
+    _require_cuda(left, right)
+    if left.shape[:-1] != right.shape[:-1]:
+        raise ValueError("dot batch shapes must match")
+    if left.dtype != right.dtype:
+        raise ValueError("dot inputs must share a storage dtype")
+    if left.shape[-1] != plan.source_size or right.shape[-1] != plan.output_size:
+        raise ValueError("dot buffer dimensions do not match layout")
+    batch_shape = left.shape[:-1]
+    batches = prod(batch_shape)
+    if out is None:
+        out = torch.empty(batch_shape, dtype=left.dtype, device=left.device)
+    if scratch is None:
+        scratch = torch.empty((max(batches, 1), plan.scratch_elements), dtype=left.dtype, device=left.device)
+    err = _native.error_buffer()
+    status = _native.lib().t0b_dot(plan._handle, _storage_code(left), left.data_ptr(), right.data_ptr(),
+                                   out.data_ptr(), batches, int(bool(conjugate_left)), scratch.data_ptr(),
+                                   plan.device_table(left.device).data_ptr(), _stream(left.device), err, len(err))
+    _native.check(status, err)
+    return out
+
+
 def axpby(alpha, x: torch.Tensor, beta, y: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     """alpha * x + beta * y elementwise (TensorMap.add)."""
     _require_cuda(x, y)

@@ -87,6 +87,23 @@ class TensorMap:
         """hom(domain, codomain) with every block conjugate-transposed."""
         return adjoint(self)
 
+    def inner(self, other: "TensorMap") -> torch.Tensor:
+        """sum over blocks of vdot(self block, other block) (tensor_map.py:457-473;
+        abelian quantum dimensions are 1): one Dot over the whole storage
+        with the left side conjugated."""
+        if self.space != other.space:
+            raise ValueError("TensorMap spaces are not compatible for inner")
+        dtype = torch.promote_types(self.data.dtype, other.data.dtype)
+        return stride.execute_dot(self.data.to(dtype).contiguous(), other.data.to(dtype).contiguous(),
+                                  _storage_dot_plan(self.space, _ELEMENT_BYTES[dtype]), conjugate_left=True)
+
+    def dot(self, other: "TensorMap") -> torch.Tensor:
+        return self.inner(other)
+
+    def norm(self) -> torch.Tensor:
+        """sqrt(real(inner(self, self))) (tensor_map.py:478-484)."""
+        return torch.sqrt(torch.real(self.inner(self)))
+
     def add(self, other: "TensorMap", alpha=1, beta=1) -> "TensorMap":
         """alpha * self + beta * other (tensor_map.py:434-455)."""
         if self.space != other.space:
@@ -95,6 +112,21 @@ class TensorMap:
         left = self.data.to(dtype)
         right = other.data.to(dtype)
         return TensorMap(self.space, stride.axpby(alpha, left.contiguous(), beta, right.contiguous()))
+
+
+_DOT_PLANS: dict = {}
+
+
+def _storage_dot_plan(space: HomSpace, element_bytes: int) -> stride.Plan:
+    """A Dot plan of one contiguous record over a space's whole storage."""
+    n = degeneracy_structure(space).total_dim
+    key = (n, element_bytes)
+    plan = _DOT_PLANS.get(key)
+    if plan is None:
+        words = stride.encode_layout([stride.AffineRecord((n,), (1,), 0, (1,), 0)], source_size=n, output_size=n)
+        plan = stride.Plan(_native.OP_DOT, words, element_bytes=element_bytes)
+        _DOT_PLANS[key] = plan
+    return plan
 
 
 def _result_dtype(left: torch.dtype, right: torch.dtype, *scalars) -> torch.dtype:

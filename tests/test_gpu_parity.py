@@ -297,3 +297,55 @@ def test_rectangular_tiles_with_edges(dtype):
     for alpha, beta in ((1.0, 1.0), (1.0, 0.0), (-2.0, 0.5), (0.0, 1.0)):
         got = host(stride.execute_update(cuda(x), cuda(base), alpha, beta, update))
         assert np.array_equal(bits(got), bits(so.update(words, x, base, real(alpha), real(beta)))), (alpha, beta)
+
+
+def dot_layout(rng, size, records=12):
+    out = []
+    for _ in range(records):
+        rank = int(rng.integers(1, 4))
+        shape = tuple(int(n) for n in rng.integers(1, 40, size=rank))
+        left = tuple(int(s) for s in rng.integers(-3, 4, size=rank))
+        right = tuple(int(s) for s in rng.integers(-3, 4, size=rank))
+
+        def origin(strides):
+            low = sum((n - 1) * s for n, s in zip(shape, strides) if s < 0)
+            high = sum((n - 1) * s for n, s in zip(shape, strides) if s > 0)
+            return int(rng.integers(-low, size - high)) if size - high > -low else None
+
+        lo, ro = origin(left), origin(right)
+        if lo is not None and ro is not None:
+            out.append(stride.AffineRecord(shape, left, lo, right, ro))
+    return out
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_dot_matches_oracle(dtype):
+    """Dot over overlapping, broadcast and negative-stride records; the error
+    is measured against the sum of |terms| (single precision sums accumulate
+    in double precision)."""
+    rng = np.random.default_rng(141)
+    size = 5000
+    records = dot_layout(rng, size)
+    words = stride.encode_layout(records, source_size=size, output_size=size)
+    a, b = sample(rng, dtype, (3, size)), sample(rng, dtype, (3, size))
+    plan = stride.Plan(_native.OP_DOT, words, element_bytes=np.dtype(dtype).itemsize)
+    for conjugate in (False, True):
+        got = host(stride.execute_dot(cuda(a), cuda(b), plan, conjugate_left=conjugate))
+        expected = so.dot(words, a, b, conjugate)
+        magnitude = so.dot(words, np.abs(a), np.abs(b))
+        assert np.all(np.abs(got - expected) <= TOL[dtype] * np.maximum(magnitude, 1e-300))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_tensormap_inner_and_norm(dtype):
+    v = space(U1Irrep, {-1: 30, 0: 40, 1: 30})
+    h = hom((v, v), (v,))
+    n = degeneracy_structure(h).total_dim
+    rng = np.random.default_rng(151)
+    x, y = sample(rng, dtype, n), sample(rng, dtype, n)
+    tx, ty = TensorMap(h, cuda(x)), TensorMap(h, cuda(y))
+    got = host(tx.inner(ty))
+    expected = np.vdot(x.astype(np.complex128), y.astype(np.complex128))
+    assert abs(got - expected) <= TOL[dtype] * np.sum(np.abs(x) * np.abs(y))
+    norm = float(host(tx.norm()))
+    assert abs(norm - np.linalg.norm(x.astype(np.complex128))) <= TOL[dtype] * np.linalg.norm(x)

@@ -142,3 +142,31 @@ def test_random_reductions_match_compiled_reference(seed, dtype):
     tolerance = 1e-6 if real == np.float32 else 1e-12
     scale = max(float(np.max(np.abs(theirs))), 1.0)
     assert float(np.max(np.abs(mine - theirs))) <= tolerance * scale
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", range(4))
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.complex64, np.complex128])
+def test_random_dots_match_compiled_reference(seed, dtype):
+    """Dot records are only bounds-checked: sides may overlap or repeat."""
+    rng = np.random.default_rng(300 + seed)
+    records = []
+    for _ in range(10):
+        rank = int(rng.integers(1, 4))
+        shape = tuple(int(n) for n in rng.integers(1, 5, size=rank))
+        left = tuple(int(s) for s in rng.integers(-3, 4, size=rank))
+        right = tuple(int(s) for s in rng.integers(-3, 4, size=rank))
+        def origin(strides):
+            low = sum((n - 1) * s for n, s in zip(shape, strides) if s < 0)
+            high = sum((n - 1) * s for n, s in zip(shape, strides) if s > 0)
+            return int(rng.integers(-low, 200 - high))
+        records.append(stride.AffineRecord(shape, left, origin(left), right, origin(right)))
+    words = stride.encode_layout(records, source_size=200, output_size=200)
+    complex_storage = np.iscomplexobj(np.zeros(1, dtype))
+    a = (rng.standard_normal((3, 200)) + (1j * rng.standard_normal((3, 200)) if complex_storage else 0)).astype(dtype)
+    b = (rng.standard_normal((3, 200)) + (1j * rng.standard_normal((3, 200)) if complex_storage else 0)).astype(dtype)
+    for conjugate in (False, True):
+        mine = so.dot(words, a, b, conjugate)
+        theirs = ref.dot(words, a, b, conjugate)
+        tolerance = 1e-5 if dtype in (np.float32, np.complex64) else 1e-12
+        assert np.max(np.abs(mine - theirs)) <= tolerance * max(1.0, float(np.max(np.abs(theirs))))
