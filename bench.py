@@ -54,6 +54,9 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=None, help="end-to-end steps (default: min(steps, 8))")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-contraction", action="store_true", help="skip the contraction TFLOP/s measurement")
+    p.add_argument("--no-trace", action="store_true", help="skip the partial-trace measurement")
+    p.add_argument("--trace-degeneracies", default="4,3",
+                   help="Z2 x U(1) trace workload degeneracies for parity 0,1 (4,3 = the benchmark; smaller for profiling)")
     p.add_argument("--scale", type=int, default=64,
                    help="leg degeneracy scale (64 = the benchmark workload; smaller values for profiling)")
     return p.parse_args()
@@ -263,6 +266,56 @@ def contraction_bench(device, steps: int, warmup: int):
             "gemm": {"kernel": "DmmaGemm (sector GEMM launch alone)", "value": round(gemm_tf, 3),
                      "ms": round(gemm_ms, 4), "peak": round(peak, 2), "frac": round(gemm_tf / peak, 4),
                      "peak_kind": "measured here: cuBLAS f64 GEMM 8192^3, best of 5"}}
+
+
+def trace_bench(device, steps: int, warmup: int, degeneracies=(4, 3)):
+    """Partial trace of the Z2 x U(1) 6-leg tensor (degeneracies 4 / 3, q in
+    -3..3: all 298,592 sub-blocks, N = 548,896,075 f64) over the leg pairs
+    (1, 4) and (2, 5) down to a 2-leg map: one reduction call (two kernels).
+    It reads only the 2744 contributing records' diagonal elements; GB/s are
+    given at 8 B per element read or written, and at the 32-byte DRAM sector
+    each scattered read occupies."""
+    import torch
+    from tensor0_b200 import _native, stride
+    from tensor0_b200.structure import ProductSector, U1Irrep, Z2Irrep, degeneracy_structure, hom, space
+    from tensor0_b200.tensor_map import trace_plan
+    w = space(ProductSector(Z2Irrep, U1Irrep), {(p, q): degeneracies[p] for p in (0, 1) for q in range(-3, 4)})
+    h = hom((w, w, w), (w, w, w))
+    n = degeneracy_structure(h).total_dim
+    tp = trace_plan(h, (1, 2), (4, 5), (0,), (3,))
+    engine = tp.engine_plan(torch.float64)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3)
+    x = torch.randn(n, generator=gen, device=device, dtype=torch.float64)
+    coefficients = torch.as_tensor(tp.coefficients, dtype=torch.float64, device=device)
+    out = torch.empty(engine.output_size, dtype=torch.float64, device=device)
+    scratch = torch.empty(engine.scratch_elements, dtype=torch.float64, device=device)
+    # Elements read: every contributing record's open x traced box.
+    words = np.asarray(tp.words, dtype=np.int64).view(np.uint64)
+    read = 0
+    at = 4
+    for _ in range(int(words[3])):
+        rank = int(words[at])
+        shape = words[at + 3: at + 3 + rank]
+        read += int(np.prod(shape))
+        at += 3 + 5 * rank
+    for _ in range(warmup):
+        stride.execute_reduction(x, engine, coefficients, out=out, scratch=scratch)
+    stream = torch.cuda.current_stream(device)
+    total, _ = timed_events(stream, steps, lambda _: stride.execute_reduction(x, engine, coefficients, out=out,
+                                                                               scratch=scratch))
+    ms = total / steps
+    algorithmic = 8 * (read + engine.output_size)
+    sectors = 32 * read + 8 * engine.output_size
+    peak, peak_kind = load_peaks()
+    return {"metric": "partial trace GB/s",
+            "workload": f"Z2xU1 6-leg deg {degeneracies[0]}/{degeneracies[1]} q=-3..3, trace (1,4),(2,5), f64",
+            "elements": n, "records": int(tp.records), "elements_read": read, "outputs": engine.output_size,
+            "ms_per_call": round(ms, 5), "kernels_per_call": engine.info["kernels_per_call"],
+            "value": round(algorithmic / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "roofline": {"bound": "hbm (scattered 8-byte reads)", "peak": peak, "peak_kind": peak_kind,
+                         "frac_at_8_bytes": round(algorithmic / (ms / 1e3) / 1e9 / peak, 5),
+                         "frac_at_32_byte_sectors": round(sectors / (ms / 1e3) / 1e9 / peak, 5)}}
 
 
 def device_uuid(index: int) -> str:
@@ -590,6 +643,10 @@ def main():
     contraction = None
     if not args.no_contraction:
         contraction = contraction_bench(device, max(args.steps, 5), args.warmup)
+    trace = None
+    if not args.no_trace:
+        trace = trace_bench(device, max(args.steps, 5), args.warmup,
+                            tuple(int(d) for d in args.trace_degeneracies.split(",")))
 
     cpu = None
     if not args.no_cpu_baseline:
@@ -615,6 +672,7 @@ def main():
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
         "contraction": contraction,
+        "trace": trace,
     }
     print(json.dumps(line), flush=True)
 

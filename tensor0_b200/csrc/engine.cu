@@ -688,16 +688,24 @@ __global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
     const int64_t batch = w / wave_tasks;
     const int64_t task = args.task_begin + (w - batch * wave_tasks);
     const ReduceGroup& g = args.groups[FindGroup(args.groups, args.group_begin, args.group_end, task, true)];
-    const int64_t local = task - g.task_begin;
-    const int64_t chunk = local / g.owners;
-    const int64_t owner = local - chunk * g.owners;
+    const uint32_t local = static_cast<uint32_t>(task - g.task_begin);
+    const uint32_t chunk = Division(g.div_owners).Div(local);
+    const uint32_t owner = local - chunk * static_cast<uint32_t>(g.owners);
     int idx[kMaxRank];
-    int64_t rem = owner;
-    for (int a = 0; a < g.rank; ++a) { idx[a] = static_cast<int>(rem % g.n[a]); rem /= g.n[a]; }
-    const int64_t first = g.rec_begin + chunk * g.chunk_records;
+    uint32_t rem = owner;
+    for (int a = 0; a < g.rank; ++a) {
+      const uint32_t next = Division(g.div_n[a]).Div(rem);
+      idx[a] = static_cast<int>(rem - next * static_cast<uint32_t>(g.n[a]));
+      rem = next;
+    }
+    const int64_t first = g.rec_begin + static_cast<int64_t>(chunk) * g.chunk_records;
     const int64_t last = min(g.rec_end, first + g.chunk_records);
+    // Lanes take (record, fiber element) pairs: lanes stride one record's
+    // fiber (lanes_per_record 32), or each lane sums whole records.
+    const int per = g.lanes_per_record;
+    const int sub = lane % per;
     T acc{};
-    for (int64_t r = first; r < last; ++r) {
+    for (int64_t r = first + lane / per; r < last; r += 32 / per) {
       const ReduceRecord& rec = args.records[r];
       C c{};
       bool one = true;
@@ -709,14 +717,13 @@ __global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
       int64_t at = rec.src_off + batch * args.src_size;
       for (int a = 0; a < rec.map_rank; ++a) at += idx[a] * rec.s[a];
       const int fr = rec.fiber_rank, mr = rec.map_rank;
-      for (int f = lane; f < rec.fiber_count; f += 32) {
+      for (int f = sub; f < rec.fiber_count; f += per) {
         int64_t off = 0;
-        int rest = f;
+        uint32_t rest = static_cast<uint32_t>(f);
         for (int a = 0; a < fr; ++a) {
-          const int n = rec.n[mr + a];
-          const int i = rest % n;
-          rest /= n;
-          off += i * rec.s[mr + a];
+          const uint32_t next = Division(rec.div_n[mr + a]).Div(rest);
+          off += static_cast<int64_t>(rest - next * static_cast<uint32_t>(rec.n[mr + a])) * rec.s[mr + a];
+          rest = next;
         }
         T value = src[at + off];
         if constexpr (Elem<T>::kComplex) {
@@ -747,8 +754,12 @@ __global__ void __launch_bounds__(kThreads) ReduceFinish(ReduceArgs args) {
     T sum = partial[0];
     for (int k = 1; k < g.chunks; ++k) sum = Add(sum, partial[static_cast<int64_t>(k) * g.owners]);
     int64_t at = g.dst_off + batch * args.out_size;
-    int64_t rem = owner;
-    for (int a = 0; a < g.rank; ++a) { at += (rem % g.n[a]) * g.d[a]; rem /= g.n[a]; }
+    uint32_t rem = static_cast<uint32_t>(owner);
+    for (int a = 0; a < g.rank; ++a) {
+      const uint32_t next = Division(g.div_n[a]).Div(rem);
+      at += static_cast<int64_t>(rem - next * static_cast<uint32_t>(g.n[a])) * g.d[a];
+      rem = next;
+    }
     out[at] = Add(out[at], sum);
   }
 }

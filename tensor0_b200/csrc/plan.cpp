@@ -623,6 +623,7 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
       }
       rr.fiber_rank = k - rr.map_rank;
       rr.fiber_count = static_cast<int32_t>(fiber_count);
+      for (int a = 0; a < kMaxRank; ++a) rr.div_n[a] = MakeDivision(static_cast<uint32_t>(std::max(rr.n[a], 1)));
       fiber_total += fiber_count;
       read_elements += fiber_count * static_cast<uint64_t>(group_owners);
       reduce_records.push_back(rr);
@@ -631,8 +632,17 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     const int64_t members = group.rec_end - group.rec_begin;
     const int64_t average = std::max<int64_t>(1, static_cast<int64_t>(fiber_total) / std::max<int64_t>(1, members));
     // Chunks of records sized for about 512 summed elements per warp task.
-    group.chunk_records = static_cast<int32_t>(std::clamp<int64_t>(CeilDiv(512, average), 1, members));
+    // Short fibers (a trace's diagonals) are summed one record per lane, so a
+    // warp's records are fetched in parallel rather than one after another.
+    group.lanes_per_record = average < 32 ? 1 : 32;
+    group.chunk_records = static_cast<int32_t>(std::clamp<int64_t>(
+        group.lanes_per_record == 1 ? 128 : CeilDiv(512, average), 1, members));
     group.chunks = static_cast<int32_t>(CeilDiv(members, group.chunk_records));
+    if (group.owners * group.chunks >= (int64_t{1} << 31)) {
+      throw std::runtime_error("a reduction group has more than 2^31 (output, chunk) tasks");
+    }
+    group.div_owners = MakeDivision(static_cast<uint32_t>(group.owners));
+    for (int a = 0; a < kMaxRank; ++a) group.div_n[a] = MakeDivision(static_cast<uint32_t>(std::max(group.n[a], 1)));
     group.task_begin = tasks;
     group.owner_begin = owners;
     group.scratch_off = scratch;

@@ -85,7 +85,9 @@ struct alignas(16) ReduceGroup {
   int64_t owner_begin;  // prefix of owners over groups (pass-2 threads)
   int64_t scratch_off;  // partial of (chunk, owner) at scratch_off + chunk * owners + owner
   int32_t chunk_records;
-  int32_t pad_;
+  int32_t lanes_per_record;              // 32: lanes stride one record's fiber; 1: each lane sums whole records
+  DivisionConstants div_owners;          // task -> (chunk, owner)
+  DivisionConstants div_n[kMaxRank];     // owner -> map indices
 };
 
 struct alignas(16) ReduceRecord {
@@ -96,6 +98,7 @@ struct alignas(16) ReduceRecord {
   int32_t fiber_rank;
   int32_t coef_slot;
   int32_t fiber_count;
+  DivisionConstants div_n[kMaxRank];     // fiber index -> fiber axis indices (fiber axes only)
 };
 
 // Dot record: axis 0 (the smallest right stride after canonicalisation) is

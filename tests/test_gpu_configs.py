@@ -277,3 +277,25 @@ def test_sector_shards_gathered_equal_the_single_launch(world):
     torch.cuda.synchronize()
     assert torch.equal(stride.execute_copy(gathered_y, unpack).view(torch.int32), y.data.view(torch.int32))
     assert torch.equal(stride.execute_copy(gathered_z, unpack).view(torch.int32), z.data.view(torch.int32))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_long_fiber_reductions(dtype):
+    """Records summing 100-300 elements each (lanes stride one record's fiber)
+    beside short-fiber records (lanes take whole records)."""
+    rng = np.random.default_rng(171)
+    records = [stride.AffineRecord((8, 100), (100, 1), 0, (1, 0), 0),
+               stride.AffineRecord((8, 300), (1, 8), 800, (1, 0), 0),
+               stride.AffineRecord((8, 3), (3, 1), 3200, (1, 0), 8),
+               stride.AffineRecord((8, 150), (150, 1), 0, (1, 0), 8)]
+    words = stride.encode_reduction_layout(records, output_shapes=[(8, 1)] * 4, reduction_axes=[(False, True)] * 4,
+                                           source_size=3300, output_size=16)
+    x = sample(rng, dtype, (2, 3300))
+    real = np.float32 if dtype in (np.float32, np.complex64) else np.float64
+    coefficients = np.array([1.0, -0.5, 2.0, 1.0], real)
+    plan = stride.Plan(_native.OP_REDUCTION, words, element_bytes=np.dtype(dtype).itemsize,
+                       coefficient_records=np.arange(4))
+    got = host(stride.execute_reduction(torch.from_numpy(x).cuda(), plan, torch.from_numpy(coefficients)))
+    expected = so.reduction(words, x, list(coefficients), np.arange(4))
+    magnitude = so.reduction(words, np.abs(x), [abs(c) for c in coefficients], np.arange(4))
+    assert np.all(np.abs(got - expected) <= 4 * TOL[dtype] * np.maximum(np.abs(magnitude), 1e-300))
