@@ -636,7 +636,7 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     // warp's records are fetched in parallel rather than one after another.
     group.lanes_per_record = average < 32 ? 1 : 32;
     group.chunk_records = static_cast<int32_t>(std::clamp<int64_t>(
-        group.lanes_per_record == 1 ? 128 : CeilDiv(512, average), 1, members));
+        group.lanes_per_record == 1 ? 32 : CeilDiv(512, average), 1, members));
     group.chunks = static_cast<int32_t>(CeilDiv(members, group.chunk_records));
     if (group.owners * group.chunks >= (int64_t{1} << 31)) {
       throw std::runtime_error("a reduction group has more than 2^31 (output, chunk) tasks");
