@@ -674,6 +674,7 @@ __device__ __forceinline__ T WarpSum(T v) {
 }
 
 // Pass 1: one warp per (owner, chunk of records); lanes stride the fibers.
+constexpr int kFiberLoads = 4;
 template <typename T, typename CA>
 __global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
   using Real = typename Elem<T>::Real;
@@ -708,28 +709,49 @@ __global__ void __launch_bounds__(kThreads) ReducePartials(ReduceArgs args) {
     for (int64_t r = first + lane / per; r < last; r += 32 / per) {
       const ReduceRecord& rec = args.records[r];
       C c{};
-      bool one = true;
+      bool one = true, zero = false;
       if (rec.coef_slot >= 0) {
         c = ReadCoefficient<Real>(static_cast<const CA*>(args.ca), rec.coef_slot, args.ca_count, batch);
-        if (IsZero(c)) continue;
-        one = IsOne(c);
       }
       int64_t at = rec.src_off + batch * args.src_size;
       for (int a = 0; a < rec.map_rank; ++a) at += idx[a] * rec.s[a];
       const int fr = rec.fiber_rank, mr = rec.map_rank;
-      for (int f = sub; f < rec.fiber_count; f += per) {
-        int64_t off = 0;
-        uint32_t rest = static_cast<uint32_t>(f);
-        for (int a = 0; a < fr; ++a) {
-          const uint32_t next = Division(rec.div_n[mr + a]).Div(rest);
-          off += static_cast<int64_t>(rest - next * static_cast<uint32_t>(rec.n[mr + a])) * rec.s[mr + a];
-          rest = next;
+      // kFiberLoads elements' loads are issued before their sums, which are
+      // added in fiber order; the coefficient is read alongside the first
+      // loads (a zero coefficient skips the record's terms, as the reference
+      // does, without a round trip ahead of the loads).
+      for (int f0 = sub; f0 < rec.fiber_count; f0 += per * kFiberLoads) {
+        T value[kFiberLoads];
+#pragma unroll
+        for (int u = 0; u < kFiberLoads; ++u) {
+          const int f = f0 + u * per;
+          value[u] = T{};
+          if (f < rec.fiber_count) {
+            int64_t off = 0;
+            uint32_t rest = static_cast<uint32_t>(f);
+            for (int a = 0; a < fr; ++a) {
+              const uint32_t next = Division(rec.div_n[mr + a]).Div(rest);
+              off += static_cast<int64_t>(rest - next * static_cast<uint32_t>(rec.n[mr + a])) * rec.s[mr + a];
+              rest = next;
+            }
+            value[u] = src[at + off];
+          }
         }
-        T value = src[at + off];
-        if constexpr (Elem<T>::kComplex) {
-          if (args.conjugate) value.y = -value.y;
+        if (f0 == sub && rec.coef_slot >= 0) {
+          zero = IsZero(c);
+          one = IsOne(c);
         }
-        acc = Add(acc, one ? value : Scale(c, value));
+        if (zero) break;
+#pragma unroll
+        for (int u = 0; u < kFiberLoads; ++u) {
+          if (f0 + u * per < rec.fiber_count) {
+            T v = value[u];
+            if constexpr (Elem<T>::kComplex) {
+              if (args.conjugate) v.y = -v.y;
+            }
+            acc = Add(acc, one ? v : Scale(c, v));
+          }
+        }
       }
     }
     acc = WarpSum(acc);
@@ -751,8 +773,17 @@ __global__ void __launch_bounds__(kThreads) ReduceFinish(ReduceArgs args) {
     const ReduceGroup& g = args.groups[FindGroup(args.groups, args.group_begin, args.group_end, owner_id, false)];
     const int64_t owner = owner_id - g.owner_begin;
     const T* partial = scratch + batch * args.scratch_stride + g.scratch_off + owner;
+    // Loads of four partials are issued before their (in-order) sums.
     T sum = partial[0];
-    for (int k = 1; k < g.chunks; ++k) sum = Add(sum, partial[static_cast<int64_t>(k) * g.owners]);
+    int k = 1;
+    for (; k + 3 < g.chunks; k += 4) {
+      const T a = partial[static_cast<int64_t>(k) * g.owners];
+      const T b = partial[static_cast<int64_t>(k + 1) * g.owners];
+      const T c = partial[static_cast<int64_t>(k + 2) * g.owners];
+      const T d = partial[static_cast<int64_t>(k + 3) * g.owners];
+      sum = Add(Add(Add(Add(sum, a), b), c), d);
+    }
+    for (; k < g.chunks; ++k) sum = Add(sum, partial[static_cast<int64_t>(k) * g.owners]);
     int64_t at = g.dst_off + batch * args.out_size;
     uint32_t rem = static_cast<uint32_t>(owner);
     for (int a = 0; a < g.rank; ++a) {
