@@ -55,6 +55,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-contraction", action="store_true", help="skip the contraction TFLOP/s measurement")
     p.add_argument("--no-trace", action="store_true", help="skip the partial-trace measurement")
+    p.add_argument("--no-grouped", action="store_true", help="skip the grouped-transform measurement")
+    p.add_argument("--grouped-extent", type=int, default=16,
+                   help="grouped workload block extent d (blocks d^4; 16 = the benchmark, smaller for profiling)")
     p.add_argument("--trace-degeneracies", default="4,3",
                    help="Z2 x U(1) trace workload degeneracies for parity 0,1 (4,3 = the benchmark; smaller for profiling)")
     p.add_argument("--scale", type=int, default=64,
@@ -299,23 +302,95 @@ def trace_bench(device, steps: int, warmup: int, degeneracies=(4, 3)):
         shape = words[at + 3: at + 3 + rank]
         read += int(np.prod(shape))
         at += 3 + 5 * rank
+    call = lambda: stride.execute_reduction(x, engine, coefficients, out=out, scratch=scratch)
     for _ in range(warmup):
-        stride.execute_reduction(x, engine, coefficients, out=out, scratch=scratch)
+        call()
     stream = torch.cuda.current_stream(device)
-    total, _ = timed_events(stream, steps, lambda _: stride.execute_reduction(x, engine, coefficients, out=out,
-                                                                               scratch=scratch))
-    ms = total / steps
+    eager, _ = timed_events(stream, steps, lambda _: call())
+    # A call is a few microseconds of device work, less than the host needs to
+    # enqueue it from Python: the device time per call is taken from a CUDA
+    # graph of `per_graph` consecutive calls (the C ABI allocates nothing and
+    # never synchronizes, so it captures as is).
+    per_graph = 20
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(per_graph):
+            call()
+    for _ in range(warmup):
+        graph.replay()
+    total, _ = timed_events(stream, steps, lambda _: graph.replay())
+    ms = total / steps / per_graph
+    del graph
     algorithmic = 8 * (read + engine.output_size)
     sectors = 32 * read + 8 * engine.output_size
     peak, peak_kind = load_peaks()
     return {"metric": "partial trace GB/s",
             "workload": f"Z2xU1 6-leg deg {degeneracies[0]}/{degeneracies[1]} q=-3..3, trace (1,4),(2,5), f64",
             "elements": n, "records": int(tp.records), "elements_read": read, "outputs": engine.output_size,
-            "ms_per_call": round(ms, 5), "kernels_per_call": engine.info["kernels_per_call"],
+            "ms_per_call": round(ms, 5), "timing": f"CUDA graph of {per_graph} calls, replayed",
+            "ms_per_call_enqueued_from_python": round(eager / steps, 5),
+            "kernels_per_call": engine.info["kernels_per_call"],
             "value": round(algorithmic / (ms / 1e3) / 1e9, 3), "unit": "GB/s",
             "roofline": {"bound": "hbm (scattered 8-byte reads)", "peak": peak, "peak_kind": peak_kind,
                          "frac_at_8_bytes": round(algorithmic / (ms / 1e3) / 1e9 / peak, 5),
                          "frac_at_32_byte_sectors": round(sectors / (ms / 1e3) / 1e9 / peak, 5)}}
+
+
+def grouped_bench(device, steps: int, warmup: int, extent: int = 16):
+    """Grouped transform of a synthetic SU(2)-like permute: 384 groups of
+    1-4 fusion trees (as many destination as source trees; 845 of each with
+    this seed) over d^4 blocks (d = 16: 65,536 f64 elements, 512 KiB per
+    block), permutation (2, 0, 3, 1), random orthogonal basis matrices,
+    packed source and destination storage of 0.44 GB each (larger than the
+    L2).  One launch per call; GB/s at one read of every source block and one
+    write of every destination block."""
+    import torch
+    from types import SimpleNamespace
+    from tensor0_b200 import _native, stride
+    rng = np.random.default_rng(5)
+    shape = (extent,) * 4
+    permutation = (2, 0, 3, 1)
+    logical = tuple(shape[p] for p in permutation)
+    count = extent ** 4
+    trees = rng.choice([1, 2, 3, 4], size=384, p=[0.3, 0.3, 0.25, 0.15])
+    sources, destinations, groups = [], [], []
+    for n in trees:
+        n = int(n)
+        q, _ = np.linalg.qr(rng.standard_normal((n, n)))
+        src = list(range(len(sources), len(sources) + n))
+        dst = list(range(len(destinations), len(destinations) + n))
+        for _ in range(n):
+            sources.append(SimpleNamespace(sizes=shape, strides=stride.contiguous_strides(shape),
+                                           offset=len(sources) * count))
+            destinations.append(SimpleNamespace(sizes=logical, strides=stride.contiguous_strides(logical),
+                                                offset=len(destinations) * count))
+        groups.append(SimpleNamespace(src_indices=tuple(src), dst_indices=tuple(dst), transform=q))
+    words, matrices = stride.encode_grouped(sources, destinations, permutation, groups,
+                                            source_size=len(sources) * count,
+                                            output_size=len(destinations) * count)
+    plan = stride.Plan(_native.OP_GROUPED, words, element_bytes=8)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    x = torch.randn(plan.source_size, generator=gen, device=device, dtype=torch.float64)
+    out = torch.empty(plan.output_size, device=device, dtype=torch.float64)
+    m = torch.from_numpy(np.concatenate(matrices).astype(np.float64)).to(device)
+    for _ in range(warmup):
+        stride.execute_grouped(x, plan, m, out=out)
+    stream = torch.cuda.current_stream(device)
+    total, _ = timed_events(stream, steps, lambda _: stride.execute_grouped(x, plan, m, out=out))
+    ms = total / steps
+    algorithmic = 8 * (plan.source_size + plan.output_size)
+    peak, peak_kind = load_peaks()
+    achieved = algorithmic / (ms / 1e3) / 1e9
+    return {"metric": "grouped transform GB/s",
+            "workload": f"SU2-like grouped permute (2,0,3,1): 384 groups of 1-4 trees, {len(sources)} blocks of "
+                        f"{extent}^4 f64 per side",
+            "groups": len(groups), "blocks": len(sources), "elements_per_side": plan.source_size,
+            "ms_per_call": round(ms, 5), "kernels_per_call": plan.info["kernels_per_call"],
+            "value": round(achieved, 3), "unit": "GB/s",
+            "roofline": {"bound": "hbm", "kernel": "GroupedKernel<double, double>", "peak": peak,
+                         "peak_kind": peak_kind, "frac": round(achieved / peak, 4),
+                         "algorithmic_bytes_per_launch": algorithmic}}
 
 
 def device_uuid(index: int) -> str:
@@ -648,6 +723,10 @@ def main():
         trace = trace_bench(device, max(args.steps, 5), args.warmup,
                             tuple(int(d) for d in args.trace_degeneracies.split(",")))
 
+    grouped = None
+    if not args.no_grouped:
+        grouped = grouped_bench(device, max(args.steps, 5), args.warmup, args.grouped_extent)
+
     cpu = None
     if not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -673,6 +752,7 @@ def main():
         "clocks": clocks.summary(),
         "contraction": contraction,
         "trace": trace,
+        "grouped": grouped,
     }
     print(json.dumps(line), flush=True)
 

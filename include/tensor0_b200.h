@@ -49,6 +49,7 @@ extern "C" {
 #define T0B_OP_DOT 2
 #define T0B_OP_ACCUMULATION 3
 #define T0B_OP_REDUCTION 4
+#define T0B_OP_GROUPED 5
 
 /* Plan flags. */
 /* The producer guarantees that distinct records write disjoint output
@@ -79,7 +80,9 @@ const char* t0b_version(void);
  *              and its destination side the right one, both only bounds-checked);
  *              T0B_OP_REDUCTION takes the reduction protocol's u64 words
  *              (little-endian bit patterns carried as i64), as the reference's
- *              Tensor0StridePrepareLayout bridge does (descriptor.cc:321-340).
+ *              Tensor0StridePrepareLayout bridge does (descriptor.cc:321-340);
+ *              T0B_OP_GROUPED takes this library's grouped-transform words
+ *              (see t0b_grouped_transform).
  *   coefficient_records: strictly increasing record indices that carry a
  *              coefficient (accumulation / reduction only; others factor 1),
  *              as the `coefficient_records` attribute (accumulation.cu:54-70).
@@ -208,6 +211,32 @@ int t0b_update(const t0b_plan* plan, int32_t dtype, const void* source, const vo
 int t0b_dot(const t0b_plan* plan, int32_t dtype, const void* left, const void* right, void* output,
             int64_t batches, int32_t conjugate_left, void* scratch, const int64_t* device_table,
             void* stream, char* error, size_t error_size);
+
+/*
+ * Grouped transform (the non-abelian permute's multi-tree groups): for each
+ * group, destination block j = sum_i M[j][i] * source block i, elementwise over
+ * one logical block shape; 1 x 1 groups follow the direct accumulation rule
+ * (0 writes +0, 1 copies, others scale).  Output elements no destination
+ * covers are zero.  The plan (T0B_OP_GROUPED, no coefficient records, no flags)
+ * takes the words
+ *   [1, source_size, output_size, groups,
+ *    per group: rank, n_src, n_dst, shape[rank],
+ *               n_src x (offset, strides[rank]),   (source strides in the shape's axis order)
+ *               n_dst x (offset, strides[rank])]
+ * with every address in bounds, each destination injective and all
+ * destinations pairwise disjoint.  matrices: t0b_plan_matrix_elements()
+ * values, each group's row-major [n_dst][n_src] matrix in group order, of the
+ * storage's real type or (complex storage) its complex type.
+ * source [batches, source_size], output [batches, output_size].
+ * Replaces the pack (copy_p) -> small dense matmul -> unpack (update_p /
+ * copy_p) sequence of _strided_grouped_transform (_stride/_tensor_ops.py:119-203).
+ */
+int t0b_grouped_transform(const t0b_plan* plan, int32_t dtype, const void* source, void* output,
+                          int64_t batches, const void* matrices, int32_t matrix_dtype,
+                          const int64_t* device_table, void* stream, char* error, size_t error_size);
+
+/* Matrix elements a grouped plan's execute call reads; 0 for other plans. */
+uint64_t t0b_plan_matrix_elements(const t0b_plan* plan);
 
 /*
  * TensorMap.add: out[i] = alpha * x[i] + beta * y[i] over n elements, with

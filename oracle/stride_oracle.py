@@ -236,3 +236,44 @@ def dot(words, left: np.ndarray, right: np.ndarray, conjugate_left: bool = False
         b = right[..., addresses(shape, dstr, do)].astype(wide)
         out = out + np.sum((np.conj(a) if conjugate_left else a) * b, axis=-1)
     return out
+
+
+def grouped(source: np.ndarray, source_blocks, destination_blocks, output_size: int, permutation, groups):
+    """Grouped transform (_strided_grouped_transform, _tensor_ops.py:119-203;
+    restated after the reference's own checker,
+    tests/stride/support/oracles/grouped.py:13-35).
+
+    ``*_blocks`` are (shape, strides, offset) sub-blocks; ``groups`` are
+    (src_indices, dst_indices, matrix).  Output starts at zero.  A 1 x 1 group
+    is the direct accumulation into zeros (factor 0 gives zeros, 1 the source
+    values, others a scaling; -0 becomes +0); a larger one multiplies its
+    [n_dst, n_src] matrix into the stacked source rows (products and sums in
+    double / complex double, rounded to the storage type once).  Each
+    destination row, reshaped to the source block shape and transposed by
+    ``permutation``, is written to its destination block.  Real storage uses
+    a matrix's real part."""
+    dtype = source.dtype
+    batch_shape = source.shape[:-1]
+    out = np.zeros((*batch_shape, output_size), dtype)
+    complex_storage = np.iscomplexobj(source)
+    for src_indices, dst_indices, matrix in groups:
+        shape = tuple(source_blocks[src_indices[0]][0])
+        rows = np.stack([source[..., addresses(*source_blocks[i])] for i in src_indices], axis=-2)
+        m = np.asarray(matrix)
+        if not complex_storage:
+            m = m.real
+        if m.shape == (1, 1):
+            # The reference runs these as accumulation records into zeros
+            # (_tensor_ops.py:168-176): 0 + c * x.
+            factor = m.reshape(())
+            mapped = (np.zeros_like(rows) if factor == 0 else _zero_plus(rows) if factor == 1
+                      else _zero_plus(_scale(factor, rows, dtype)))
+        else:
+            wide = np.complex128 if complex_storage else np.float64
+            mapped = np.einsum("ji,...ik->...jk", m.astype(wide), rows.astype(wide)).astype(dtype)
+        for row, index in enumerate(dst_indices):
+            shaped = mapped[..., row, :].reshape((*batch_shape, *shape))
+            axes = (*range(len(batch_shape)), *(len(batch_shape) + axis for axis in permutation))
+            values = np.transpose(shaped, axes).reshape((*batch_shape, int(np.prod(shape))))
+            out[..., addresses(*destination_blocks[index])] = values
+    return out

@@ -14,7 +14,7 @@ from . import build as _build
 LIBRARY_PATH = _build.LIBRARY
 
 S32, F32, F64, C64, C128 = 4, 11, 12, 15, 18
-OP_COPY, OP_UPDATE, OP_DOT, OP_ACCUMULATION, OP_REDUCTION = 0, 1, 2, 3, 4
+OP_COPY, OP_UPDATE, OP_DOT, OP_ACCUMULATION, OP_REDUCTION, OP_GROUPED = 0, 1, 2, 3, 4, 5
 PLAN_OUTPUTS_DISJOINT = 1
 PLAN_WIDE_OFFSETS = 2
 PLAN_CONJUGATE_SOURCE = 4
@@ -66,6 +66,10 @@ SIGNATURES = {
     "t0b_dot": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                ctypes.c_char_p, ctypes.c_size_t]),
+    "t0b_grouped_transform": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                             ctypes.c_int64, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                                             ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "t0b_plan_matrix_elements": (ctypes.c_uint64, [ctypes.c_void_p]),
     "t0b_axpby": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64, ctypes.c_double, ctypes.c_double,
                                  ctypes.c_void_p, ctypes.c_double, ctypes.c_double, ctypes.c_void_p,
                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_char_p, ctypes.c_size_t]),

@@ -11,7 +11,17 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "plan.h"
+
 namespace t0b {
+
+// Division by a constant computed on the host (MakeDivision).
+struct FastDiv {
+  uint32_t m, l;
+  __device__ __forceinline__ uint32_t Div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
+};
+
+__device__ __forceinline__ FastDiv Division(const DivisionConstants& c) { return FastDiv{c.magic, c.shift}; }
 
 template <typename T> struct Elem;
 template <> struct Elem<float>   { using Real = float;  static constexpr bool kComplex = false; };

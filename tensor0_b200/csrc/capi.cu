@@ -273,9 +273,15 @@ void t0b_plan_query(const t0b_plan* plan, t0b_plan_info* info) {
   info->output_size = p.output_size;
   info->records = p.records;
   info->tiles = p.map_tiles;
-  info->kernels_per_call = p.operation == 2 ? 2 : (p.has_map ? 1 : 0) + 2 * p.waves.size();
+  info->kernels_per_call = p.operation == 2   ? 2
+                           : p.operation == 5 ? (p.grouped_units != 0 ? 1 : 0)
+                                              : (p.has_map ? 1 : 0) + 2 * p.waves.size();
   info->full_coverage = p.full_coverage ? 1 : 0;
   info->bytes_moved = p.bytes_moved;
+}
+
+uint64_t t0b_plan_matrix_elements(const t0b_plan* plan) {
+  return plan != nullptr && plan->plan.operation == 5 ? plan->plan.coefficient_rows : 0;
 }
 
 uint64_t t0b_plan_created_count(void) { return g_created.load(std::memory_order_relaxed); }
@@ -418,6 +424,49 @@ int t0b_dot(const t0b_plan* plan, int32_t dtype, const void* left, const void* r
     args.right_size = static_cast<int64_t>(p.output_size);
     args.conjugate_left = conjugate_left;
     t0b::LaunchDot(dtype, args, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int t0b_grouped_transform(const t0b_plan* plan, int32_t dtype, const void* source, void* output,
+                          int64_t batches, const void* matrices, int32_t matrix_dtype,
+                          const int64_t* device_table, void* stream, char* error, size_t error_size) {
+  return Guard(error, error_size, [&] {
+    RequirePlan(plan, 5, dtype, batches);
+    const auto& p = plan->plan;
+    const int eb = p.element_bytes;
+    const uint64_t b = static_cast<uint64_t>(batches);
+    const uint64_t out_bytes = Bytes(b * p.output_size, eb);
+    const uint64_t src_bytes = Bytes(b * p.source_size, eb);
+    if (matrix_dtype == T0B_S32) throw t0b::InvalidArgument("grouped matrices must be floating point");
+    const int mb = CoefficientBytes(matrix_dtype, dtype);
+    const uint64_t matrix_bytes = Bytes(p.coefficient_rows, mb);
+    if (b == 0 || p.output_size == 0) return;
+    if (output == nullptr) throw t0b::InvalidArgument("output buffer is null");
+    if (p.source_size != 0 && source == nullptr) throw t0b::InvalidArgument("source buffer is null");
+    if (p.coefficient_rows != 0 && matrices == nullptr) throw t0b::InvalidArgument("grouped matrix buffer is null");
+    if (device_table == nullptr) throw t0b::InvalidArgument("device descriptor table is null");
+    RequireTableAligned(device_table);
+    RequireAligned(source, eb, "source");
+    RequireAligned(output, eb, "output");
+    RequireAligned(matrices, mb, "grouped matrix");
+    Disjoint(source, src_bytes, output, out_bytes);
+    Disjoint(matrices, matrix_bytes, output, out_bytes);
+    Disjoint(device_table, p.table.size() * sizeof(int64_t), output, out_bytes);
+    const auto launch_stream = static_cast<cudaStream_t>(stream);
+    if (!p.full_coverage) t0b::Check(cudaMemsetAsync(output, 0, out_bytes, launch_stream), "memset");
+    const auto& h = Header(plan);
+    t0b::GroupedArgs args{};
+    args.groups = reinterpret_cast<const t0b::GroupedGroup*>(device_table + h.grouped_offset);
+    args.operands = reinterpret_cast<const t0b::GroupedOperand*>(device_table + h.operand_offset);
+    args.ngroups = h.grouped;
+    args.units = h.grouped_units;
+    args.batches = batches;
+    args.src = source;
+    args.out = output;
+    args.matrices = matrices;
+    args.src_size = static_cast<int64_t>(p.source_size);
+    args.out_size = static_cast<int64_t>(p.output_size);
+    t0b::LaunchGrouped(dtype, matrix_dtype, args, static_cast<int64_t>(p.grouped_stage) * eb, launch_stream);
   });
 }
 

@@ -44,13 +44,6 @@ constexpr int kWarps = kThreads / 32;
 #define T0B_UPDATE_MIN_BLOCKS 3
 #endif
 
-// Division by a constant computed on the host (MakeDivision).
-struct FastDiv {
-  uint32_t m, l;
-  __device__ __forceinline__ uint32_t Div(uint32_t n) const { return (__umulhi(n, m) + n) >> l; }
-};
-
-__device__ __forceinline__ FastDiv Division(const DivisionConstants& c) { return FastDiv{c.magic, c.shift}; }
 
 // "Division" by 2^31: every run index of a single-plane run list is in plane 0.
 constexpr FastDiv kSinglePlane{0, 31};
@@ -909,15 +902,6 @@ __global__ void __launch_bounds__(kThreads) AxpbyKernel(int64_t n, S alpha, cons
   }
 }
 
-int SmCount() {
-  static int count = [] {
-    int device = 0, sms = 148;
-    if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    return sms;
-  }();
-  return count;
-}
-
 template <int Op, typename T, typename CA, typename CB, typename Off>
 void LaunchMapKernel(const MapArgs& args, int smem, cudaStream_t stream) {
   auto kernel = MapKernel<Op, T, CA, CB, Off>;
@@ -974,6 +958,15 @@ void WithStorage(int32_t dtype, F&& f) {
 }
 
 }  // namespace
+
+int SmCount() {
+  static int count = [] {
+    int device = 0, sms = 148;
+    if (cudaGetDevice(&device) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms;
+  }();
+  return count;
+}
 
 void Check(cudaError_t status, const char* what) {
   if (status != cudaSuccess) {

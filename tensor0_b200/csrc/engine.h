@@ -67,7 +67,23 @@ struct DotArgs {
   int conjugate_left;
 };
 
+struct GroupedArgs {
+  const GroupedGroup* groups;
+  const GroupedOperand* operands;
+  int64_t ngroups;
+  int64_t units;                    // per batch
+  int64_t batches;
+  const void* src;
+  void* out;
+  const void* matrices;             // row-major [n_dst][n_src] per group, in group order
+  int64_t src_size;
+  int64_t out_size;
+};
+
 extern std::atomic<uint64_t> g_kernel_launches;
+
+// Multiprocessors of the current device.
+int SmCount();
 
 // Throw std::runtime_error for a failed CUDA runtime call.
 void Check(cudaError_t status, const char* what);
@@ -81,6 +97,11 @@ void LaunchMap(int op, int32_t dtype, int32_t ca_dtype, int32_t cb_dtype, const 
                int smem, bool wide, cudaStream_t stream);
 void LaunchReduce(int32_t dtype, int32_t ca_dtype, const ReduceArgs& args, cudaStream_t stream);
 void LaunchDot(int32_t dtype, const DotArgs& args, cudaStream_t stream);
+// One launch of the grouped-transform kernel; matrix_dtype is the storage's
+// real type or (complex storage) its complex type; stage_bytes is the dynamic
+// shared memory of a tiled unit (the plan's grouped_stage elements).
+void LaunchGrouped(int32_t dtype, int32_t matrix_dtype, const GroupedArgs& args, int64_t stage_bytes,
+                   cudaStream_t stream);
 void LaunchAxpby(int32_t dtype, int64_t n, double ar, double ai, const void* x, double br, double bi,
                  const void* y, void* out, cudaStream_t stream);
 

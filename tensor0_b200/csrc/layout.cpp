@@ -135,6 +135,16 @@ class WordReader {
 
 }  // namespace
 
+void CheckSide(const Record& record, bool source, uint64_t size, bool injective) {
+  const uint64_t count = ElementCount(record);
+  int64_t low = 0, high = 0;
+  AddressBounds(record, source, count == 0 ? std::vector<std::size_t>{} : AllAxes(record.shape.size()), &low, &high);
+  if ((count == 0 && static_cast<uint64_t>(high) > size) || (count != 0 && static_cast<uint64_t>(high) >= size)) {
+    throw InvalidArgument(std::string(Side(source)) + " address exceeds storage");
+  }
+  if (injective && count != 0) ProveInjective(record, source, AllAxes(record.shape.size()));
+}
+
 Layout DecodeLayout(const int64_t* words, std::size_t word_count, Validation validation) {
   if (words == nullptr && word_count != 0) throw InvalidArgument("layout descriptor is null");
   WordReader reader(words, word_count);

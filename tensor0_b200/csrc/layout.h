@@ -47,6 +47,12 @@ Layout DecodeLayout(const int64_t* words, std::size_t word_count, Validation val
 Layout DecodeReductionLayout(const int64_t* words, std::size_t word_count);
 
 uint64_t ElementCount(const Record& record);
+
+// One side of a record against its storage: every address in [0, size)
+// (an empty record's offset may equal size).  With `injective`, the side's
+// strides must also prove distinct addresses.  Throws InvalidArgument with
+// the layout decoder's messages.
+void CheckSide(const Record& record, bool source, uint64_t size, bool injective);
 bool CheckedMul(uint64_t a, uint64_t b, uint64_t* out);
 bool CheckedAdd(uint64_t a, uint64_t b, uint64_t* out);
 uint64_t AbsStride(int64_t stride);

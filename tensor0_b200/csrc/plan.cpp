@@ -444,6 +444,207 @@ Plan BuildDotPlan(const int64_t* words, std::size_t word_count, int32_t element_
   return plan;
 }
 
+// Grouped transform words (this engine's format; the reference builds pack
+// and unpack records instead, _stride/_tensor_ops.py:119-203):
+//   [1, source_size, output_size, groups,
+//    per group: rank, n_src, n_dst, shape[rank],
+//               n_src x (offset, strides[rank]),   source strides in the shape's axis order
+//               n_dst x (offset, strides[rank])]
+// Every address is bounds-checked; each destination must be injective and
+// all destinations pairwise disjoint (the producer's "complete disjoint
+// output selections").
+Plan BuildGroupedPlan(const int64_t* words, std::size_t word_count, int32_t element_bytes, uint32_t flags) {
+  if (words == nullptr && word_count != 0) throw InvalidArgument("grouped descriptor is null");
+  std::size_t cursor = 0;
+  auto next = [&]() {
+    if (cursor == word_count) throw InvalidArgument("grouped descriptor is truncated");
+    return words[cursor++];
+  };
+  auto size = [&]() {
+    const int64_t value = next();
+    if (value < 0) throw InvalidArgument("grouped size, count or offset is negative");
+    return value;
+  };
+  if (next() != 1) throw InvalidArgument("unsupported grouped descriptor version");
+  Plan plan;
+  plan.operation = 5;
+  plan.element_bytes = element_bytes;
+  plan.flags = flags;
+  plan.source_size = static_cast<uint64_t>(size());
+  plan.output_size = static_cast<uint64_t>(size());
+  const int64_t group_count = size();
+  if (static_cast<uint64_t>(group_count) > (word_count - cursor) / 3) {
+    throw InvalidArgument("grouped group count exceeds descriptor length");
+  }
+  std::vector<GroupedGroup> groups;
+  std::vector<GroupedOperand> operands;
+  std::vector<Record> destinations;
+  int64_t units = 0, matrix = 0;
+  uint64_t covered = 0, read = 0;
+  auto pow2 = [](uint64_t n) { int32_t t = 1; while (t < 32 && static_cast<uint64_t>(t) < n) t <<= 1; return t; };
+  for (int64_t index = 0; index < group_count; ++index) {
+    const int64_t rank = size();
+    const int64_t n_src = size();
+    const int64_t n_dst = size();
+    if (n_src < 1 || n_dst < 1) throw InvalidArgument("a group needs at least one source and one destination");
+    if (n_src > 4096 || n_dst > 4096) throw InvalidArgument("groups are limited to 4096 sources and destinations");
+    // The group needs rank shape words and (1 + rank) words per operand.
+    const uint64_t operand_count = static_cast<uint64_t>(n_src + n_dst);
+    const uint64_t remaining = word_count - cursor;
+    if (remaining < operand_count || static_cast<uint64_t>(rank) > (remaining - operand_count) / (1 + operand_count)) {
+      throw InvalidArgument("grouped rank exceeds descriptor length");
+    }
+    Record shape_record;
+    shape_record.shape.resize(rank);
+    for (auto& extent : shape_record.shape) extent = static_cast<uint64_t>(size());
+    shape_record.fiber.assign(rank, 0);
+    const uint64_t elements = ElementCount(shape_record);
+    std::vector<Record> sides;   // sources (src_* fields), then destinations (dst_* fields)
+    for (int64_t k = 0; k < n_src + n_dst; ++k) {
+      Record side = shape_record;
+      const bool source = k < n_src;
+      const int64_t offset = size();
+      std::vector<int64_t> strides(rank);
+      for (auto& stride : strides) stride = next();
+      if (source) { side.src_off = offset; side.sstr = strides; side.dstr.assign(rank, 0); }
+      else { side.dst_off = offset; side.dstr = strides; side.sstr.assign(rank, 0); }
+      CheckSide(side, source, source ? plan.source_size : plan.output_size, !source);
+      sides.push_back(std::move(side));
+    }
+    matrix += n_src * n_dst;
+    if (elements == 0) continue;
+    for (int64_t k = n_src; k < n_src + n_dst; ++k) destinations.push_back(sides[k]);
+    // Device axis order: extent-1 axes dropped, the first destination's
+    // smallest stride innermost; neighbouring axes contiguous in every
+    // operand fused.
+    const Record& first = sides[n_src];
+    std::vector<std::size_t> axes;
+    for (std::size_t a = 0; a < shape_record.shape.size(); ++a) if (shape_record.shape[a] > 1) axes.push_back(a);
+    std::stable_sort(axes.begin(), axes.end(), [&](std::size_t a, std::size_t b) {
+      return AbsStride(first.dstr[a]) < AbsStride(first.dstr[b]);
+    });
+    auto stride_of = [&](const Record& side, bool source, std::size_t a) { return source ? side.sstr[a] : side.dstr[a]; };
+    std::vector<uint64_t> extents;
+    std::vector<std::vector<int64_t>> strides(n_src + n_dst);
+    for (std::size_t a : axes) {
+      bool fuse = !extents.empty();
+      for (int64_t k = 0; k < n_src + n_dst && fuse; ++k) {
+        fuse = stride_of(sides[k], k < n_src, a) == strides[k].back() * static_cast<int64_t>(extents.back());
+      }
+      if (fuse && extents.back() * shape_record.shape[a] <= kExtentLimit) {
+        extents.back() *= shape_record.shape[a];
+        continue;
+      }
+      extents.push_back(shape_record.shape[a]);
+      for (int64_t k = 0; k < n_src + n_dst; ++k) strides[k].push_back(stride_of(sides[k], k < n_src, a));
+    }
+    if (extents.empty()) {
+      extents.push_back(1);
+      for (auto& list : strides) list.push_back(0);
+    }
+    if (extents.size() > static_cast<std::size_t>(kMaxRank)) {
+      throw InvalidArgument("grouped blocks with more than eight non-unit axes are unsupported");
+    }
+    for (uint64_t extent : extents) {
+      if (extent > kExtentLimit) throw InvalidArgument("grouped block extent exceeds 2^30");
+    }
+    // Tiled when the first source's smallest stride is not along X: Y, its
+    // innermost axis, becomes axis 1.
+    int y_axis = -1;
+    if (extents.size() >= 2) {
+      std::size_t best = 0;
+      for (std::size_t a = 1; a < extents.size(); ++a) {
+        if (AbsStride(strides[0][a]) < AbsStride(strides[0][best])) best = a;
+      }
+      if (best != 0) y_axis = static_cast<int>(best);
+    }
+    GroupedGroup g{};
+    if (y_axis > 0) {
+      const int32_t tx = pow2(extents[0]), ty = pow2(extents[y_axis]);
+      // The third tile axis (the next axis in device order, if any) grows the
+      // tile to about 2048 elements within the shared-memory budget.
+      int32_t tz = 1;
+      const uint64_t z_extent = extents.size() >= 3 ? extents[y_axis == 1 ? 2 : 1] : 1;
+      while (tz < 8 && static_cast<uint64_t>(tz) < z_extent && tx * ty * tz * 2 <= 2048 &&
+             n_src * 2 * tz * ty * (tx + 1) * element_bytes <= kGroupedStageBytes) {
+        tz <<= 1;
+      }
+      const int64_t stage = n_src * tz * ty * (tx + 1);
+      if (stage * element_bytes <= kGroupedStageBytes && n_src + n_dst <= kTiledOperands) {
+        g.tiled = 1;
+        g.tx = tx;
+        g.ty = ty;
+        g.tz = tz;
+        plan.grouped_stage = std::max<uint64_t>(plan.grouped_stage, static_cast<uint64_t>(stage));
+        auto move = [&](auto& list) {
+          auto value = list[y_axis];
+          list.erase(list.begin() + y_axis);
+          list.insert(list.begin() + 1, value);
+        };
+        move(extents);
+        for (auto& list : strides) move(list);
+      }
+    }
+    g.unit_begin = units;
+    g.elements = static_cast<int64_t>(elements);
+    g.operand_begin = static_cast<int64_t>(operands.size());
+    g.matrix_offset = matrix - n_src * n_dst;
+    g.rank = static_cast<int32_t>(extents.size());
+    g.n_src = static_cast<int32_t>(n_src);
+    g.n_dst = static_cast<int32_t>(n_dst);
+    for (int a = 0; a < kMaxRank; ++a) {
+      g.n[a] = a < g.rank ? static_cast<int32_t>(extents[a]) : 1;
+      g.div_n[a] = MakeDivision(static_cast<uint32_t>(g.n[a]));
+    }
+    int64_t group_units = CeilDiv(static_cast<int64_t>(elements), kGroupedTile);
+    if (g.tiled) {
+      g.tiles_x = static_cast<int32_t>(CeilDiv(g.n[0], g.tx));
+      g.tiles_y = static_cast<int32_t>(CeilDiv(g.n[1], g.ty));
+      g.tiles_z = static_cast<int32_t>(CeilDiv(g.n[2], g.tz));
+      g.div_tiles_x = MakeDivision(static_cast<uint32_t>(g.tiles_x));
+      g.div_tiles_y = MakeDivision(static_cast<uint32_t>(g.tiles_y));
+      g.div_tiles_z = MakeDivision(static_cast<uint32_t>(g.tiles_z));
+      group_units = static_cast<int64_t>(g.tiles_x) * g.tiles_y * g.tiles_z;
+      for (int a = 3; a < g.rank; ++a) group_units *= g.n[a];
+    }
+    for (int64_t k = 0; k < n_src + n_dst; ++k) {
+      GroupedOperand op{};
+      op.offset = k < n_src ? sides[k].src_off : sides[k].dst_off;
+      for (int a = 0; a < kMaxRank; ++a) op.s[a] = a < g.rank ? strides[k][a] : 0;
+      operands.push_back(op);
+    }
+    units += group_units;
+    if (units >= (int64_t{1} << 31)) throw std::runtime_error("a grouped transform spans more than 2^31 tiles per batch");
+    covered += elements * static_cast<uint64_t>(n_dst);
+    read += elements * static_cast<uint64_t>(n_src);
+    groups.push_back(g);
+  }
+  if (cursor != word_count) throw InvalidArgument("grouped descriptor has trailing words");
+  std::vector<const Record*> pointers;
+  for (const Record& record : destinations) pointers.push_back(&record);
+  if (!ProveDisjoint(pointers, plan.output_size)) {
+    throw InvalidArgument("grouped destinations are not pairwise disjoint");
+  }
+  plan.records = static_cast<uint64_t>(group_count);
+  plan.coefficient_rows = static_cast<uint64_t>(matrix);
+  plan.grouped_units = static_cast<uint64_t>(units);
+  plan.full_coverage = covered == plan.output_size;
+  plan.bytes_moved = (read + plan.output_size) * static_cast<uint64_t>(element_bytes);
+  TableHeader header{};
+  header.version = kTableVersion;
+  plan.table.assign(sizeof(TableHeader) / sizeof(int64_t), 0);
+  header.grouped = static_cast<int64_t>(groups.size());
+  header.grouped_offset = static_cast<int64_t>(plan.table.size());
+  Append(plan.table, groups);
+  header.operand_offset = static_cast<int64_t>(plan.table.size());
+  Append(plan.table, operands);
+  header.grouped_units = units;
+  header.map_offset = header.group_offset = header.reduce_offset = header.dot_offset =
+      static_cast<int64_t>(plan.table.size());
+  std::memcpy(plan.table.data(), &header, sizeof(header));
+  return plan;
+}
+
 }  // namespace
 
 Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
@@ -456,6 +657,11 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
     if (coefficient_count != 0) throw InvalidArgument("dot plans take no coefficient records");
     if ((flags & 4u) != 0) throw InvalidArgument("source conjugation is supported for accumulation and reduction plans");
     return BuildDotPlan(words, word_count, element_bytes, flags);
+  }
+  if (operation == 5) {
+    if (coefficient_count != 0) throw InvalidArgument("grouped plans take their matrices at execution, not coefficient records");
+    if (flags != 0) throw InvalidArgument("grouped plans take no flags");
+    return BuildGroupedPlan(words, word_count, element_bytes, flags);
   }
   Layout layout;
   switch (operation) {

@@ -121,6 +121,42 @@ struct alignas(16) DotRecord {
 // Partial sums per batch of the dot engine's first pass.
 constexpr int64_t kDotPartials = 1184;
 
+// Grouped transform: a group maps n_src source blocks of one logical shape
+// through an [n_dst][n_src] matrix to n_dst destination blocks.  Axes are in
+// the device order: axis 0 (X) has the smallest destination stride.  An
+// element group's unit is kGroupedTile consecutive block elements, one per
+// thread.  A tiled group (one whose first source is not innermost along X)
+// puts the source's innermost axis second (Y); its unit is a tx x ty x tz
+// tile of (X, Y, axis 2) at one index of the remaining axes, read along Y
+// into shared memory and written along X out of it.
+constexpr int32_t kGroupedTile = 256;
+constexpr int64_t kGroupedStageBytes = 96 * 1024;   // shared memory of one tiled unit, at most
+constexpr int32_t kTiledOperands = 64;              // sources + destinations of a tiled group, at most
+
+struct alignas(16) GroupedGroup {
+  int64_t unit_begin;       // first unit of this group within one batch
+  int64_t elements;         // block elements
+  int64_t operand_begin;    // first GroupedOperand: n_src sources, then n_dst destinations
+  int64_t matrix_offset;    // element offset of the group's row-major [n_dst][n_src] matrix
+  int32_t n[kMaxRank];      // extents
+  int32_t rank;
+  int32_t n_src;
+  int32_t n_dst;
+  int32_t tiled;            // 1: staged (X, Y, Z) tiles
+  int32_t tx, ty, tz;       // tile extents (powers of two; tx, ty at most 32, tz at most 8)
+  int32_t tiles_x, tiles_y, tiles_z;
+  DivisionConstants div_n[kMaxRank];   // element (or, tiled, remaining-axes index) -> axis indices
+  DivisionConstants div_tiles_x;
+  DivisionConstants div_tiles_y;
+  DivisionConstants div_tiles_z;
+  int32_t pad_[2];
+};
+
+struct alignas(16) GroupedOperand {
+  int64_t offset;
+  int64_t s[kMaxRank];      // strides in the group's axis order
+};
+
 struct TableHeader {
   int64_t version;          // kTableVersion
   int64_t map_records;
@@ -136,10 +172,13 @@ struct TableHeader {
   int64_t dot_records;
   int64_t dot_offset;
   int64_t dot_units;        // units per batch
-  int64_t reserved[2];
+  int64_t grouped;          // grouped-transform groups
+  int64_t grouped_offset;   // word offset of the GroupedGroup array
+  int64_t operand_offset;   // word offset of the GroupedOperand array
+  int64_t grouped_units;    // units per batch
 };
 
-constexpr int64_t kTableVersion = 0x7430620002;
+constexpr int64_t kTableVersion = 0x7430620003;
 
 struct Wave {               // consecutive groups that may run concurrently
   int64_t group_begin, group_end;
@@ -166,6 +205,8 @@ struct Plan {
   uint64_t scratch = 0;
   uint64_t bytes_moved = 0;      // algorithmic bytes of one batch
   uint64_t dot_units = 0;        // dot plans: work units per batch
+  uint64_t grouped_units = 0;    // grouped plans: work units per batch
+  uint64_t grouped_stage = 0;    // grouped plans: shared-memory elements of a tiled unit
   std::vector<Wave> waves;       // reduce-engine waves, in order
   std::vector<int64_t> table;    // packed device table (host words)
 };

@@ -150,6 +150,7 @@ class Plan:
         self._lib.t0b_plan_query(handle, ctypes.byref(info))
         self.info = {name: int(getattr(info, name)) for name, _ in _native.PlanInfo._fields_}
         self.scratch_elements = int(self._lib.t0b_plan_scratch_elements(handle))
+        self.matrix_elements = int(self._lib.t0b_plan_matrix_elements(handle))
         self._device_tables: dict[int, torch.Tensor] = {}
 
     @property
@@ -326,6 +327,103 @@ def execute_dot(left: torch.Tensor, right: torch.Tensor, plan: Plan, *, conjugat
                                    plan.device_table(left.device).data_ptr(), _stream(left.device), err, len(err))
     _native.check(status, err)
     return out
+
+
+def encode_grouped(source_blocks, destination_blocks, permutation, groups, *, source_size: int,
+                   output_size: int) -> tuple[np.ndarray, list[np.ndarray]]:
+    """Grouped-transform words and the groups' matrices, from the reference's
+    inputs (_strided_grouped_transform, _stride/_tensor_ops.py:119-203).
+
+    ``*_blocks`` are sub-blocks with ``sizes``, ``strides`` and ``offset``;
+    ``groups`` carry ``src_indices``, ``dst_indices`` and ``transform``
+    ([n_dst, n_src]).  Every group's destination blocks have the source block
+    shape permuted by ``permutation``; the source strides are permuted into
+    that order, as the reference's unpack records are."""
+    permutation = tuple(int(p) for p in permutation)
+    words = [1, int(source_size), int(output_size), len(groups)]
+    matrices = []
+    for group in groups:
+        src_indices = tuple(int(i) for i in group.src_indices)
+        dst_indices = tuple(int(i) for i in group.dst_indices)
+        matrix = np.asarray(group.transform)
+        if matrix.shape != (len(dst_indices), len(src_indices)):
+            raise ValueError("generic tree transform matrix shape does not match its trees")
+        source_sizes = tuple(int(n) for n in source_blocks[src_indices[0]].sizes)
+        if sorted(permutation) != list(range(len(source_sizes))):
+            raise ValueError("permutation does not match the source subblock rank")
+        for index in src_indices:
+            if tuple(int(n) for n in source_blocks[index].sizes) != source_sizes:
+                raise ValueError("generic tree transform source subblock shapes are inconsistent")
+        logical_shape = tuple(source_sizes[p] for p in permutation)
+        for index in dst_indices:
+            if tuple(int(n) for n in destination_blocks[index].sizes) != logical_shape:
+                raise ValueError("generic tree transform destination subblock shapes are inconsistent")
+        words += [len(logical_shape), len(src_indices), len(dst_indices), *logical_shape]
+        for index in src_indices:
+            block = source_blocks[index]
+            strides = tuple(int(s) for s in block.strides)
+            words += [int(block.offset), *(strides[p] for p in permutation)]
+        for index in dst_indices:
+            block = destination_blocks[index]
+            words += [int(block.offset), *(int(s) for s in block.strides)]
+        matrices.append(matrix.reshape(-1))
+    return np.asarray(words, dtype=np.int64), matrices
+
+
+def execute_grouped(source: torch.Tensor, plan: Plan, matrices: torch.Tensor, *,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """One grouped-transform launch over [..., source_size] storage; ``matrices``
+    holds every group's row-major matrix in group order on the device."""
+    _require_cuda(source, matrices)
+    if source.shape[-1] != plan.source_size:
+        raise ValueError("grouped buffer dimensions do not match layout")
+    if matrices.numel() != plan.matrix_elements:
+        raise ValueError("grouped matrix count does not match the plan")
+    batch_shape = source.shape[:-1]
+    batches = prod(batch_shape)
+    if out is None:
+        out = torch.empty((*batch_shape, plan.output_size), dtype=source.dtype, device=source.device)
+    matrix_code = _STORAGE.get(matrices.dtype)
+    if matrix_code is None:
+        raise ValueError("grouped matrices must be F32/F64/C64/C128")
+    err = _native.error_buffer()
+    status = _native.lib().t0b_grouped_transform(
+        plan._handle, _storage_code(source), source.data_ptr(), out.data_ptr(), batches, matrices.data_ptr(),
+        matrix_code, plan.device_table(source.device).data_ptr(), _stream(source.device), err, len(err))
+    _native.check(status, err)
+    return out
+
+
+_GROUPED_PLANS: dict[tuple[bytes, int], Plan] = {}
+
+
+def grouped_transform(source: torch.Tensor, source_layout, destination_layout, result_dtype, permutation,
+                      data) -> torch.Tensor:
+    """The reference's _strided_grouped_transform (_tensor_ops.py:119-203) in
+    one launch: single-tree groups follow the direct accumulation rule and
+    multi-tree groups multiply their basis matrix into the source blocks.
+    Storage keeps its dtype (F32/F64/C64/C128); ``result_dtype`` must be it."""
+    if result_dtype is not None and torch.empty(0, dtype=source.dtype).numpy().dtype != np.dtype(result_dtype):
+        raise NotImplementedError("the CUDA grouped transform keeps the storage dtype")
+    element_bytes = source.element_size()
+    words, matrices = encode_grouped(source_layout.subblockstructure, destination_layout.subblockstructure,
+                                     permutation, data, source_size=source.shape[-1],
+                                     output_size=destination_layout.total_dim)
+    key = (words.tobytes(), element_bytes)
+    plan = _GROUPED_PLANS.get(key)
+    if plan is None:
+        plan = Plan(_native.OP_GROUPED, words, element_bytes=element_bytes)
+        if len(_GROUPED_PLANS) > 256:
+            _GROUPED_PLANS.clear()
+        _GROUPED_PLANS[key] = plan
+    flat = np.concatenate(matrices) if matrices else np.zeros(0)
+    single = source.dtype in (torch.float32, torch.complex64)
+    if source.is_complex() and np.iscomplexobj(flat):
+        flat = flat.astype(np.complex64 if single else np.complex128)
+    else:
+        flat = np.real(flat).astype(np.float32 if single else np.float64)
+    device_matrices = torch.from_numpy(np.ascontiguousarray(flat)).to(source.device)
+    return execute_grouped(source, plan, device_matrices)
 
 
 def axpby(alpha, x: torch.Tensor, beta, y: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
