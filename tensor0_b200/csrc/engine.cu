@@ -15,6 +15,7 @@
 #include "engine.h"
 
 #include "arith.cuh"
+#include "copy_async.cuh"
 
 #include <algorithm>
 #include <atomic>
@@ -354,17 +355,6 @@ __device__ __forceinline__ T LoadShared(uint32_t addr) {
   return v;
 }
 
-// Asynchronous global -> shared copy of one element (no register round trip).
-// The copies are ordered against shared-memory reads by the wait on their
-// cp.async group and the CTA barrier that follows it.
-template <int Bytes>
-__device__ __forceinline__ void CopyAsync(uint32_t smem, const void* gmem) {
-  if constexpr (Bytes == 16) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem), "l"(gmem));
-  } else {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(smem), "l"(gmem), "n"(Bytes));
-  }
-}
 
 
 // Rectangular tiles.  Every element of the box goes through shared memory at

@@ -11,9 +11,9 @@
 //
 // Element groups (the first source innermost along X, the destination's
 // innermost axis) give a thread one element.  Tiled groups stage a
-// tx x ty x tz tile of every source in shared memory, read with lanes along
-// Y (the source's innermost axis), and write every destination with lanes
-// along X.  A CTA walks a contiguous range of units, so the group is looked
+// tx x ty x tz tile of every source in shared memory with asynchronous
+// copies, lanes along Y (the source's innermost axis), and write every
+// destination with lanes along X.  A CTA walks a contiguous range of units, so the group is looked
 // up once and then advanced.
 //
 // Single-tree groups (1 x 1 matrices) follow the reference's direct path,
@@ -22,6 +22,7 @@
 #include "engine.h"
 
 #include "arith.cuh"
+#include "copy_async.cuh"
 
 #include <algorithm>
 
@@ -30,7 +31,6 @@ namespace {
 
 constexpr int kGroupedThreads = kGroupedTile;
 constexpr int kSourceRegisters = 4;   // element groups with up to this many sources keep them in registers
-constexpr int kStageLoads = 4;        // loads in flight per thread while a tile is staged
 
 template <typename T, typename M>
 __device__ __forceinline__ T Term(M m, T v) { return Scale(m, v); }
@@ -151,32 +151,22 @@ __global__ void __launch_bounds__(kGroupedThreads) GroupedKernel(GroupedArgs arg
       const int plane_shift = tx_shift + ty_shift;
       const int tile_shift = plane_shift + __ffs(g.tz) - 1;
       const int rows = 1 << (tile_shift - tx_shift);   // (axis 2, Y) rows of one source's stage
-      // Load: lanes along Y, then X, then axis 2; kStageLoads loads per
-      // thread are issued before their shared-memory stores.
+      // Load: lanes along Y, then X, then axis 2, as asynchronous copies into
+      // shared memory: a thread's whole share of the tile is in flight at once.
       const int items = n_src << tile_shift;
-      for (int k0 = threadIdx.x; k0 < items; k0 += kStageLoads * kGroupedThreads) {
-        T value[kStageLoads];
-        int slot[kStageLoads];
-#pragma unroll
-        for (int v = 0; v < kStageLoads; ++v) {
-          const int k = k0 + v * kGroupedThreads;
-          slot[v] = -1;
-          if (k < items) {
-            const int i = k >> tile_shift;
-            const int within = k & ((1 << tile_shift) - 1);
-            const int lz = within >> plane_shift;
-            const int lx = (within >> ty_shift) & (tx - 1), ly = within & (ty - 1);
-            if (lx < wx && ly < wy && lz < wz) {
-              value[v] = src[tile_base[i] + lx * tile_sx[i] + ly * tile_sy[i] + lz * tile_sz[i]];
-              slot[v] = (i * rows + (lz << ty_shift) + ly) * pitch + lx;
-            }
-          }
-        }
-#pragma unroll
-        for (int v = 0; v < kStageLoads; ++v) {
-          if (slot[v] >= 0) stage[slot[v]] = value[v];
+      const uint32_t stage_s = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
+      for (int k = threadIdx.x; k < items; k += kGroupedThreads) {
+        const int i = k >> tile_shift;
+        const int within = k & ((1 << tile_shift) - 1);
+        const int lz = within >> plane_shift;
+        const int lx = (within >> ty_shift) & (tx - 1), ly = within & (ty - 1);
+        if (lx < wx && ly < wy && lz < wz) {
+          const int slot = (i * rows + (lz << ty_shift) + ly) * pitch + lx;
+          CopyAsync<sizeof(T)>(stage_s + static_cast<uint32_t>(slot * sizeof(T)),
+                               src + tile_base[i] + lx * tile_sx[i] + ly * tile_sy[i] + lz * tile_sz[i]);
         }
       }
+      asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
       __syncthreads();
       // Combine and store: lanes along X, then Y, then axis 2.
       for (int k = threadIdx.x; k < (1 << tile_shift); k += kGroupedThreads) {

@@ -562,11 +562,12 @@ Plan BuildGroupedPlan(const int64_t* words, std::size_t word_count, int32_t elem
     if (y_axis > 0) {
       const int32_t tx = pow2(extents[0]), ty = pow2(extents[y_axis]);
       // The third tile axis (the next axis in device order, if any) grows the
-      // tile to about 2048 elements within the shared-memory budget.
+      // tile to at most 2048 elements while the stage stays small enough for
+      // several CTAs per SM.
       int32_t tz = 1;
       const uint64_t z_extent = extents.size() >= 3 ? extents[y_axis == 1 ? 2 : 1] : 1;
       while (tz < 8 && static_cast<uint64_t>(tz) < z_extent && tx * ty * tz * 2 <= 2048 &&
-             n_src * 2 * tz * ty * (tx + 1) * element_bytes <= kGroupedStageBytes) {
+             n_src * 2 * tz * ty * (tx + 1) * element_bytes <= kGroupedGrowBytes) {
         tz <<= 1;
       }
       const int64_t stage = n_src * tz * ty * (tx + 1);

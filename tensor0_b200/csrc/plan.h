@@ -131,6 +131,7 @@ constexpr int64_t kDotPartials = 1184;
 // into shared memory and written along X out of it.
 constexpr int32_t kGroupedTile = 256;
 constexpr int64_t kGroupedStageBytes = 96 * 1024;   // shared memory of one tiled unit, at most
+constexpr int64_t kGroupedGrowBytes = 40 * 1024;    // the third tile axis grows while the stage fits this
 constexpr int32_t kTiledOperands = 64;              // sources + destinations of a tiled group, at most
 
 struct alignas(16) GroupedGroup {

@@ -92,9 +92,9 @@ def test_plan_counts_and_coverage():
 
 
 def test_tiled_and_element_groups():
-    """A transposing permute of d^4 blocks is tiled 16 x 16 x 8 (X = the
-    destination's innermost axis, Y = the source's); an identity permute
-    of contiguous blocks runs one element per thread."""
+    """A transposing permute of d^4 blocks is tiled 16 x 16 x 8 for one f64
+    source (X = the destination's innermost axis, Y = the source's); an
+    identity permute of contiguous blocks runs one element per thread."""
     shape = (16,) * 4
     for permutation, tiled in (((2, 0, 3, 1), (4, 1, 1, 1, 16, 16, 8)), ((0, 1, 2, 3), None)):
         logical = tuple(shape[p] for p in permutation)
