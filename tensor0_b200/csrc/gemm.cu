@@ -6,8 +6,11 @@
 // persistent grid.
 //
 // F64 and C128 use the FP64 tensor-core MMA (mma.sync m8n8k4 f64, "DMMA");
-// C128 uses four real products per complex product.  F32 / C64 use FP32 FMA.
-// Operands are staged with cp.async (zero-filled at edges) in two stages.
+// C128 uses four real products per complex product; operands are staged with
+// cp.async (zero-filled at edges) in two stages.  F32 uses the 5th-generation
+// tensor cores (tcgen05.mma kind::tf32, accumulators in tensor memory) with a
+// three-term TF32 split, each 32-deep slice of K summed in FP32 registers
+// (TcGemm).  C64 uses FP32 FMA.
 #include "gemm.h"
 
 #include "engine.h"
@@ -271,6 +274,224 @@ __global__ void __launch_bounds__(kGemmThreads) FmaGemm(const int64_t* __restric
   }
 }
 
+// ---------------------------------------------------------------------------
+// FP32 on tcgen05 (kind::tf32).  A CTA of 128 threads owns 128 x 64 output
+// tiles (the table's second tile prefix).  Each operand value x is split into
+// hi = tf32(x) and lo = tf32(x - hi); a 32-deep K slice issues, per 8-deep MMA
+// step, lo(A) hi(B) + hi(A) lo(B) + hi(A) hi(B) into one of two tensor-memory
+// accumulators (the dropped lo lo term is below 2^-22 relative).  The tensor
+// core's accumulation over long K is not IEEE: measured 2e-6 (K = 256) and
+// 7e-6 (K = 1000) relative error when all of K stays in tensor memory.  So
+// every slice starts from zero and is added into FP32 registers: thread r
+// reads tensor-memory lane r (its output row) after the slice's MMAs
+// complete, while the next slice's MMAs run into the other accumulator.
+// Shared-memory tiles are K-major without swizzle: 16-byte chunks of four k
+// values, chunk-major over the tile's rows (leading byte offset = one chunk of
+// all rows, stride byte offset = 8 rows).
+constexpr int kTcM = 128, kTcN = 64, kTcK = 32;
+constexpr int kTcThreads = 128;
+constexpr uint32_t kTcABytes = kTcM * kTcK * 4;   // 16 KB: one part (hi or lo) of an A slice
+constexpr uint32_t kTcBBytes = kTcN * kTcK * 4;   // 8 KB
+constexpr uint32_t kTcStageBytes = 2 * kTcABytes + 2 * kTcBBytes;
+constexpr int kTcSmem = 2 * kTcStageBytes;        // two stages: 96 KB
+constexpr uint32_t kTcTmemColumns = 2 * kTcN;     // two accumulators
+constexpr uint32_t kTcSpinLimit = 1u << 24;       // mbarrier polls before a wait gives up
+
+__device__ __forceinline__ uint32_t Tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t SmemDescriptor(uint32_t addr, uint32_t leading, uint32_t stride) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFF) | (static_cast<uint64_t>((leading >> 4) & 0x3FFF) << 16) |
+         (static_cast<uint64_t>((stride >> 4) & 0x3FFF) << 32) | (uint64_t{1} << 46);
+}
+
+__device__ __forceinline__ void MmaTf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+  const uint32_t mask = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n"
+      :: "r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(mask));
+}
+
+// Bounded wait for an mbarrier phase; false if it gave up.
+__device__ __forceinline__ bool WaitPhase(uint32_t mbar, uint32_t parity) {
+  for (uint32_t i = 0; i < kTcSpinLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done) : "r"(mbar), "r"(parity) : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void TmemLoad32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+struct TcTask {
+  int64_t m, n, k, a, b, c, m0, n0;
+};
+
+__device__ __forceinline__ TcTask DecodeTcTask(const int64_t* table, int64_t sectors, int64_t tile) {
+  int64_t lo = 0, hi = sectors - 1;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (table[mid * kGemmRow + 7] <= tile) lo = mid; else hi = mid - 1;
+  }
+  const int64_t* row = table + lo * kGemmRow;
+  TcTask t;
+  t.m = row[0]; t.n = row[1]; t.k = row[2];
+  t.a = row[3]; t.b = row[4]; t.c = row[5];
+  const int64_t local = tile - row[7];
+  const int64_t tiles_n = (t.n + kTcN - 1) / kTcN;
+  t.m0 = (local / tiles_n) * kTcM;
+  t.n0 = (local % tiles_n) * kTcN;
+  return t;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restrict__ table, int64_t sectors,
+                                                       int64_t tiles, const float* __restrict__ left,
+                                                       const float* __restrict__ right, float* out) {
+  extern __shared__ __align__(1024) unsigned char tc_smem[];
+  __shared__ __align__(8) uint64_t mbar_storage[2];
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t smem = static_cast<uint32_t>(__cvta_generic_to_shared(tc_smem));
+  const uint32_t mbar0 = static_cast<uint32_t>(__cvta_generic_to_shared(&mbar_storage[0]));
+  if (warp == 0) {
+    const uint32_t slot = static_cast<uint32_t>(__cvta_generic_to_shared(&tmem_slot));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(slot), "r"(kTcTmemColumns));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(mbar0));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(mbar0 + 8));
+    asm volatile("fence.mbarrier_init.release.cluster;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = tmem_slot;
+  // kind::tf32, F32 accumulate, A and B K-major, N = 64, M = 128.
+  const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kTcN >> 3) << 17) | ((kTcM >> 4) << 24);
+  uint32_t parity[2] = {0, 0};
+  bool ok = true;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const TcTask t = DecodeTcTask(table, sectors, tile);
+    float acc[kTcN];
+#pragma unroll
+    for (int j = 0; j < kTcN; ++j) acc[j] = 0.0f;
+    const int64_t slices = (t.k + kTcK - 1) / kTcK;
+    // Add slice `s`'s accumulator (buffer s & 1) into the registers.
+    auto drain = [&](int64_t s) {
+      const int buf = static_cast<int>(s & 1);
+      ok = WaitPhase(mbar0 + 8 * buf, parity[buf]) && ok;
+      parity[buf] ^= 1u;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+      for (int c0 = 0; c0 < kTcN; c0 += 32) {
+        float v[32];
+        TmemLoad32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(buf * kTcN + c0), v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
+      }
+    };
+    for (int64_t s = 0; s < slices; ++s) {
+      const int buf = static_cast<int>(s & 1);
+      const uint32_t a_hi = smem + buf * kTcStageBytes, a_lo = a_hi + kTcABytes;
+      const uint32_t b_hi = a_lo + kTcABytes, b_lo = b_hi + kTcBBytes;
+      const int64_t k0 = s * kTcK;
+      // A slice: a warp covers 8 rows x one 4-value chunk (coalesced 16-byte
+      // pieces; one contiguous 128-byte run of shared memory).
+      for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
+        const int k_in = e & 3, m_lo = (e >> 2) & 7, chunk = (e >> 5) & 7, m_hi = e >> 8;
+        const int m = m_hi * 8 + m_lo, k = chunk * 4 + k_in;
+        const int64_t row = t.m0 + m, col = k0 + k;
+        const float x = (row < t.m && col < t.k) ? left[t.a + row * t.k + col] : 0.0f;
+        const uint32_t hi = Tf32(x), lo = Tf32(x - __uint_as_float(hi));
+        const uint32_t off = ((static_cast<uint32_t>(chunk) * kTcM + m) << 4) + (k_in << 2);
+        asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_hi + off), "r"(hi));
+        asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_lo + off), "r"(lo));
+      }
+      // B slice, transposed to K-major: a warp covers 8 columns x 4 k rows.
+      for (int e = tid; e < kTcN * kTcK; e += kTcThreads) {
+        const int l = e & 31, w = e >> 5;
+        const int n = (w & 7) * 8 + (l & 7), k_in = l >> 3, chunk = w >> 3;
+        const int64_t row = k0 + chunk * 4 + k_in, col = t.n0 + n;
+        const float x = (row < t.k && col < t.n) ? right[t.b + row * t.n + col] : 0.0f;
+        const uint32_t hi = Tf32(x), lo = Tf32(x - __uint_as_float(hi));
+        const uint32_t off = ((static_cast<uint32_t>(chunk) * kTcN + n) << 4) + (k_in << 2);
+        asm volatile("st.shared.b32 [%0], %1;" :: "r"(b_hi + off), "r"(hi));
+        asm volatile("st.shared.b32 [%0], %1;" :: "r"(b_lo + off), "r"(lo));
+      }
+      asm volatile("fence.proxy.async.shared::cta;");
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncthreads();
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      if (tid == 0) {
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * kTcN);
+#pragma unroll
+        for (int step = 0; step < kTcK / 8; ++step) {
+          const uint32_t a_step = static_cast<uint32_t>(step) * 2 * kTcM * 16;
+          const uint32_t b_step = static_cast<uint32_t>(step) * 2 * kTcN * 16;
+          const uint64_t ah = SmemDescriptor(a_hi + a_step, kTcM * 16, 128);
+          const uint64_t al = SmemDescriptor(a_lo + a_step, kTcM * 16, 128);
+          const uint64_t bh = SmemDescriptor(b_hi + b_step, kTcN * 16, 128);
+          const uint64_t bl = SmemDescriptor(b_lo + b_step, kTcN * 16, 128);
+          MmaTf32(d, al, bh, idesc, step == 0 ? 0u : 1u);
+          MmaTf32(d, ah, bl, idesc, 1u);
+          MmaTf32(d, ah, bh, idesc, 1u);
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     :: "r"(mbar0 + 8 * buf) : "memory");
+      }
+      // While slice s runs on the tensor cores, fold slice s - 1 into the
+      // registers; its stage and accumulator are then free for slice s + 1.
+      if (s > 0) drain(s - 1);
+    }
+    if (slices > 0) drain(slices - 1);
+    // Epilogue: thread r writes row m0 + r.  A wait that gave up (the
+    // tensor cores never signalled) leaves NaN in the tile instead of a
+    // partial sum.
+    if (!ok) {
+#pragma unroll
+      for (int j = 0; j < kTcN; ++j) acc[j] = __int_as_float(0x7fc00000);
+    }
+    const int64_t row = t.m0 + warp * 32 + lane;
+    if (row < t.m) {
+      float* dst = out + t.c + row * t.n + t.n0;
+      const int64_t width = t.n - t.n0 < kTcN ? t.n - t.n0 : kTcN;
+#pragma unroll
+      for (int j = 0; j < kTcN; ++j) {
+        if (j < width) dst[j] = acc[j];
+      }
+    }
+    // Every thread's tensor-memory reads of this tile precede the next
+    // tile's MMAs into the same accumulators.
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(kTcTmemColumns));
+}
+
 int SmCountGemm() {
   static int count = [] {
     int device = 0, sms = 148;
@@ -283,14 +504,15 @@ int SmCountGemm() {
 }  // namespace
 
 void BuildGemmTable(int64_t sectors, const int64_t* spec, int64_t* table) {
-  int64_t tiles = 0;
+  int64_t tiles = 0, tc_tiles = 0;
   for (int64_t s = 0; s < sectors; ++s) {
     const int64_t* in = spec + s * 6;
     int64_t* row = table + s * kGemmRow;
     for (int i = 0; i < 6; ++i) row[i] = in[i];
     row[6] = tiles;
-    row[7] = 0;
+    row[7] = tc_tiles;
     tiles += ((in[0] + kTile - 1) / kTile) * ((in[1] + kTile - 1) / kTile);
+    tc_tiles += ((in[0] + kTcM - 1) / kTcM) * ((in[1] + kTcN - 1) / kTcN);
   }
 }
 
@@ -323,7 +545,7 @@ void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const
     }
     return count;
   };
-  int64_t tiles = 0;
+  int64_t tiles = 0, tc_tiles = 0;
   std::vector<std::pair<int64_t, int64_t>> blocks;
   blocks.reserve(static_cast<std::size_t>(sectors));
   for (int64_t s = 0; s < sectors; ++s) {
@@ -334,7 +556,9 @@ void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const
     if (row[0] > (int64_t{1} << 31) || row[1] > (int64_t{1} << 31) || row[2] > (int64_t{1} << 40)) {
       throw InvalidArgument("GEMM block extents are too large");
     }
-    if (row[6] != tiles) throw InvalidArgument("GEMM table tile prefix is inconsistent; build it with t0b_gemm_table_build");
+    if (row[6] != tiles || row[7] != tc_tiles) {
+      throw InvalidArgument("GEMM table tile prefix is inconsistent; build it with t0b_gemm_table_build");
+    }
     const uint64_t c_count = span(row[5], row[0], row[1], output_size, "output");
     if (row[2] != 0) {
       span(row[3], row[0], row[2], left_size, "left");
@@ -342,6 +566,7 @@ void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const
     }
     if (c_count != 0) blocks.emplace_back(row[5], row[5] + static_cast<int64_t>(c_count));
     tiles += ((row[0] + kTile - 1) / kTile) * ((row[1] + kTile - 1) / kTile);
+    tc_tiles += ((row[0] + kTcM - 1) / kTcM) * ((row[1] + kTcN - 1) / kTcN);
   }
   std::sort(blocks.begin(), blocks.end());
   for (std::size_t i = 1; i < blocks.size(); ++i) {
@@ -381,11 +606,14 @@ void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const
           device_table, sectors, tiles, static_cast<const double*>(left), static_cast<const double*>(right),
           static_cast<double*>(output));
       break;
-    case 11:
-      FmaGemm<false><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
-          device_table, sectors, tiles, static_cast<const float*>(left), static_cast<const float*>(right),
+    case 11: {
+      Check(cudaFuncSetAttribute(TcGemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem), "tcgen05 GEMM shared memory");
+      const int64_t tc_grid = std::min<int64_t>(tc_tiles, int64_t{SmCountGemm()} * 2);
+      TcGemm<<<static_cast<unsigned>(tc_grid), kTcThreads, kTcSmem, stream>>>(
+          device_table, sectors, tc_tiles, static_cast<const float*>(left), static_cast<const float*>(right),
           static_cast<float*>(output));
       break;
+    }
     case 15:
       FmaGemm<true><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
           device_table, sectors, tiles, static_cast<const float*>(left), static_cast<const float*>(right),

@@ -7,7 +7,9 @@
 
 namespace t0b {
 
-// Device table row: {m, n, k, a_off, b_off, c_off, tile_begin, 0}.
+// Device table row: {m, n, k, a_off, b_off, c_off, tile_begin, tc_tile_begin}:
+// prefixes over sectors of 64 x 64 tiles (DMMA and FMA kernels) and of
+// 128 x 64 tiles (the tcgen05 FP32 kernel).
 constexpr int kGemmRow = 8;
 
 void BuildGemmTable(int64_t sectors, const int64_t* spec, int64_t* table);

@@ -228,6 +228,25 @@ def test_sector_gemm(dtype):
     assert_close(got, so.sector_gemm(np.array(spec), left, right, c_off), dtype)
 
 
+def test_sector_gemm_f32_long_k_on_tensor_cores():
+    """F32 sectors run on tcgen05 (three-term TF32 split, 32-deep K slices
+    summed in FP32 registers): the error stays within the f32 tolerance for
+    K in the thousands, several 128 x 64 tiles per sector and ragged edges."""
+    rng = np.random.default_rng(33)
+    shapes = [(300, 200, 2048), (129, 65, 1000), (7, 3, 4097)]
+    spec, a_off, b_off, c_off = [], 0, 0, 0
+    for m, n, k in shapes:
+        spec.append((m, n, k, a_off, b_off, c_off))
+        a_off, b_off, c_off = a_off + m * k, b_off + k * n, c_off + m * n
+    left, right = sample(rng, np.float32, a_off), sample(rng, np.float32, b_off)
+    plan = stride.GemmPlan(np.array(spec))
+    for _ in range(2):
+        out = torch.full((c_off,), float("nan"), dtype=torch.float32, device="cuda")
+        got = host(stride.sector_gemm(plan, cuda(left), cuda(right), out))
+        expected = so.sector_gemm(np.array(spec), left.astype(np.float64), right.astype(np.float64), c_off)
+        assert_close(got, expected, np.float32)
+
+
 @pytest.mark.parametrize("dtype", [np.float64, np.complex128])
 def test_dmrg_contraction(dtype):
     """L . A with U1 sectors (the DMRG-style contraction, reduced bond dimension)."""
