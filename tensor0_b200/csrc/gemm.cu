@@ -284,12 +284,13 @@ __global__ void __launch_bounds__(kGemmThreads) FmaGemm(const int64_t* __restric
 // 7e-6 (K = 1000) relative error when all of K stays in tensor memory.  So
 // every slice starts from zero and is added into FP32 registers: thread r
 // reads tensor-memory lane r (its output row) after the slice's MMAs
-// complete, while the next slice's MMAs run into the other accumulator.
+// complete.  Two stages: slice s + 1 is copied (cp.async) while slice s is
+// split and multiplied, and the two accumulators alternate.
 // Shared-memory tiles are K-major without swizzle: 16-byte chunks of four k
 // values, chunk-major over the tile's rows (leading byte offset = one chunk of
 // all rows, stride byte offset = 8 rows).
 constexpr int kTcM = 128, kTcN = 64, kTcK = 32;
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 256;   // warp w drains lanes 32 (w % 4).. and columns 32 (w / 4)..
 constexpr uint32_t kTcABytes = kTcM * kTcK * 4;   // 16 KB: one part (hi or lo) of an A slice
 constexpr uint32_t kTcBBytes = kTcN * kTcK * 4;   // 8 KB
 constexpr uint32_t kTcStageBytes = 2 * kTcABytes + 2 * kTcBBytes;
@@ -301,6 +302,11 @@ __device__ __forceinline__ uint32_t Tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
+}
+
+// Asynchronous 4-byte copy into shared memory; zero-filled when !valid.
+__device__ __forceinline__ void TcCopy4(uint32_t dst, const float* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
 }
 
 __device__ __forceinline__ uint64_t SmemDescriptor(uint32_t addr, uint32_t leading, uint32_t stride) {
@@ -371,6 +377,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
   __shared__ __align__(8) uint64_t mbar_storage[2];
   __shared__ uint32_t tmem_slot;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;   // tensor-memory lane quarter, accumulator column half
   const uint32_t smem = static_cast<uint32_t>(__cvta_generic_to_shared(tc_smem));
   const uint32_t mbar0 = static_cast<uint32_t>(__cvta_generic_to_shared(&mbar_storage[0]));
   if (warp == 0) {
@@ -393,9 +400,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
   bool ok = true;
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
     const TcTask t = DecodeTcTask(table, sectors, tile);
-    float acc[kTcN];
+    float acc[32];
 #pragma unroll
-    for (int j = 0; j < kTcN; ++j) acc[j] = 0.0f;
+    for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
     const int64_t slices = (t.k + kTcK - 1) / kTcK;
     // Add slice `s`'s accumulator (buffer s & 1) into the registers.
     auto drain = [&](int64_t s) {
@@ -403,47 +410,91 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
       ok = WaitPhase(mbar0 + 8 * buf, parity[buf]) && ok;
       parity[buf] ^= 1u;
       asm volatile("tcgen05.fence::after_thread_sync;");
+      float v[32];
+      TmemLoad32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * kTcN + half * 32), v);
 #pragma unroll
-      for (int c0 = 0; c0 < kTcN; c0 += 32) {
-        float v[32];
-        TmemLoad32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(buf * kTcN + c0), v);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c0 + j] = __fadd_rn(acc[c0 + j], v[j]);
-      }
+      for (int j = 0; j < 32; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
     };
-    for (int64_t s = 0; s < slices; ++s) {
-      const int buf = static_cast<int>(s & 1);
-      const uint32_t a_hi = smem + buf * kTcStageBytes, a_lo = a_hi + kTcABytes;
-      const uint32_t b_hi = a_lo + kTcABytes, b_lo = b_hi + kTcBBytes;
+    // Slice s lands in stage s & 1: raw values by cp.async at their K-major
+    // positions in the hi buffers; each thread then splits the values it
+    // copied itself (hi in place, lo beside it).  A warp's A piece is 8 rows x
+    // one 4-value chunk (coalesced 16-byte pieces, one contiguous 128-byte run
+    // of shared memory); its B piece is 8 columns x 4 k rows.
+    auto a_position = [&](int e, int& m, int& k) -> uint32_t {
+      const int k_in = e & 3, m_lo = (e >> 2) & 7, chunk = (e >> 5) & 7, m_hi = e >> 8;
+      m = m_hi * 8 + m_lo;
+      k = chunk * 4 + k_in;
+      return ((static_cast<uint32_t>(chunk) * kTcM + m) << 4) + (k_in << 2);
+    };
+    auto b_position = [&](int e, int& n, int& k) -> uint32_t {
+      const int l = e & 31, w = e >> 5;
+      const int k_in = l >> 3, chunk = w >> 3;
+      n = (w & 7) * 8 + (l & 7);
+      k = chunk * 4 + k_in;
+      return ((static_cast<uint32_t>(chunk) * kTcN + n) << 4) + (k_in << 2);
+    };
+    auto issue = [&](int64_t s) {
+      const uint32_t a_hi = smem + static_cast<uint32_t>(s & 1) * kTcStageBytes;
+      const uint32_t b_hi = a_hi + 2 * kTcABytes;
       const int64_t k0 = s * kTcK;
-      // A slice: a warp covers 8 rows x one 4-value chunk (coalesced 16-byte
-      // pieces; one contiguous 128-byte run of shared memory).
       for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
-        const int k_in = e & 3, m_lo = (e >> 2) & 7, chunk = (e >> 5) & 7, m_hi = e >> 8;
-        const int m = m_hi * 8 + m_lo, k = chunk * 4 + k_in;
+        int m, k;
+        const uint32_t off = a_position(e, m, k);
         const int64_t row = t.m0 + m, col = k0 + k;
-        const float x = (row < t.m && col < t.k) ? left[t.a + row * t.k + col] : 0.0f;
+        const bool valid = row < t.m && col < t.k;
+        TcCopy4(a_hi + off, valid ? left + t.a + row * t.k + col : left, valid);
+      }
+      for (int e = tid; e < kTcN * kTcK; e += kTcThreads) {
+        int n, k;
+        const uint32_t off = b_position(e, n, k);
+        const int64_t row = k0 + k, col = t.n0 + n;
+        const bool valid = row < t.k && col < t.n;
+        TcCopy4(b_hi + off, valid ? right + t.b + row * t.n + col : right, valid);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto split = [&](int64_t s) {
+      const uint32_t a_hi = smem + static_cast<uint32_t>(s & 1) * kTcStageBytes;
+      const uint32_t a_lo = a_hi + kTcABytes, b_hi = a_lo + kTcABytes, b_lo = b_hi + kTcBBytes;
+      for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
+        int m, k;
+        const uint32_t off = a_position(e, m, k);
+        float x;
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(a_hi + off));
         const uint32_t hi = Tf32(x), lo = Tf32(x - __uint_as_float(hi));
-        const uint32_t off = ((static_cast<uint32_t>(chunk) * kTcM + m) << 4) + (k_in << 2);
         asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_hi + off), "r"(hi));
         asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_lo + off), "r"(lo));
       }
-      // B slice, transposed to K-major: a warp covers 8 columns x 4 k rows.
       for (int e = tid; e < kTcN * kTcK; e += kTcThreads) {
-        const int l = e & 31, w = e >> 5;
-        const int n = (w & 7) * 8 + (l & 7), k_in = l >> 3, chunk = w >> 3;
-        const int64_t row = k0 + chunk * 4 + k_in, col = t.n0 + n;
-        const float x = (row < t.k && col < t.n) ? right[t.b + row * t.n + col] : 0.0f;
+        int n, k;
+        const uint32_t off = b_position(e, n, k);
+        float x;
+        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(b_hi + off));
         const uint32_t hi = Tf32(x), lo = Tf32(x - __uint_as_float(hi));
-        const uint32_t off = ((static_cast<uint32_t>(chunk) * kTcN + n) << 4) + (k_in << 2);
         asm volatile("st.shared.b32 [%0], %1;" :: "r"(b_hi + off), "r"(hi));
         asm volatile("st.shared.b32 [%0], %1;" :: "r"(b_lo + off), "r"(lo));
       }
+    };
+    if (slices > 0) issue(0);
+    for (int64_t s = 0; s < slices; ++s) {
+      const int buf = static_cast<int>(s & 1);
+      // Slice s - 1's MMAs are done once its accumulator is drained, so its
+      // stage (the one slice s + 1 uses) is free.
+      if (s > 0) drain(s - 1);
+      if (s + 1 < slices) {
+        issue(s + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      split(s);
       asm volatile("fence.proxy.async.shared::cta;");
       asm volatile("tcgen05.fence::before_thread_sync;");
       __syncthreads();
       asm volatile("tcgen05.fence::after_thread_sync;");
       if (tid == 0) {
+        const uint32_t a_hi = smem + static_cast<uint32_t>(buf) * kTcStageBytes, a_lo = a_hi + kTcABytes;
+        const uint32_t b_hi = a_lo + kTcABytes, b_lo = b_hi + kTcBBytes;
         const uint32_t d = tmem + static_cast<uint32_t>(buf * kTcN);
 #pragma unroll
         for (int step = 0; step < kTcK / 8; ++step) {
@@ -460,24 +511,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                      :: "r"(mbar0 + 8 * buf) : "memory");
       }
-      // While slice s runs on the tensor cores, fold slice s - 1 into the
-      // registers; its stage and accumulator are then free for slice s + 1.
-      if (s > 0) drain(s - 1);
     }
     if (slices > 0) drain(slices - 1);
-    // Epilogue: thread r writes row m0 + r.  A wait that gave up (the
+    // Epilogue: a thread writes 32 columns of row m0 + 32 (w % 4) + lane.  A wait that gave up (the
     // tensor cores never signalled) leaves NaN in the tile instead of a
     // partial sum.
     if (!ok) {
 #pragma unroll
-      for (int j = 0; j < kTcN; ++j) acc[j] = __int_as_float(0x7fc00000);
+      for (int j = 0; j < 32; ++j) acc[j] = __int_as_float(0x7fc00000);
     }
-    const int64_t row = t.m0 + warp * 32 + lane;
+    const int64_t row = t.m0 + quarter * 32 + lane;
     if (row < t.m) {
-      float* dst = out + t.c + row * t.n + t.n0;
-      const int64_t width = t.n - t.n0 < kTcN ? t.n - t.n0 : kTcN;
+      float* dst = out + t.c + row * t.n + t.n0 + half * 32;
+      const int64_t width = t.n - t.n0 - half * 32;
 #pragma unroll
-      for (int j = 0; j < kTcN; ++j) {
+      for (int j = 0; j < 32; ++j) {
         if (j < width) dst[j] = acc[j];
       }
     }
