@@ -393,6 +393,38 @@ def grouped_bench(device, steps: int, warmup: int, extent: int = 16):
                          "algorithmic_bytes_per_launch": algorithmic}}
 
 
+def gemm_f32_bench(device, steps: int, warmup: int, size: int = 4096):
+    """One f32 sector of size^3 through the tcgen05 GEMM (three-term TF32
+    split, FP32 register accumulation per 32-deep slice) beside cuBLAS FP32
+    (TF32 off) on the same operands; TFLOP/s at 2 size^3 per call."""
+    import torch
+    from tensor0_b200 import stride
+    plan = stride.GemmPlan(np.array([(size, size, size, 0, 0, 0)]))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    left = torch.randn(size * size, generator=gen, device=device)
+    right = torch.randn(size * size, generator=gen, device=device)
+    out = torch.empty(size * size, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        stride.sector_gemm(plan, left, right, out)
+    total, _ = timed_events(stream, steps, lambda _: stride.sector_gemm(plan, left, right, out))
+    a, b = left.view(size, size), right.view(size, size)
+    previous = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    for _ in range(warmup):
+        torch.matmul(a, b)
+    reference, _ = timed_events(stream, steps, lambda _: torch.matmul(a, b))
+    torch.backends.cuda.matmul.allow_tf32 = previous
+    flops = 2.0 * size ** 3
+    error = float((out.view(size, size).double() - a.double() @ b.double()).abs().max()
+                  / (a.double() @ b.double()).abs().max())
+    return {"metric": "f32 sector GEMM TFLOP/s", "kernel": "TcGemm (tcgen05.mma kind::tf32, 3 terms)",
+            "shape": f"{size}^3", "ms_per_call": round(total / steps, 4),
+            "value": round(flops / (total / steps / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "cublas_fp32": round(flops / (reference / steps / 1e3) / 1e12, 2), "max_relative_error": error}
+
+
 def device_uuid(index: int) -> str:
     import torch
     try:
@@ -723,6 +755,10 @@ def main():
         trace = trace_bench(device, max(args.steps, 5), args.warmup,
                             tuple(int(d) for d in args.trace_degeneracies.split(",")))
 
+    gemm_f32 = None
+    if not args.no_contraction:
+        gemm_f32 = gemm_f32_bench(device, max(args.steps, 5), args.warmup)
+
     grouped = None
     if not args.no_grouped:
         grouped = grouped_bench(device, max(args.steps, 5), args.warmup, args.grouped_extent)
@@ -753,6 +789,7 @@ def main():
         "contraction": contraction,
         "trace": trace,
         "grouped": grouped,
+        "gemm_f32": gemm_f32,
     }
     print(json.dumps(line), flush=True)
 

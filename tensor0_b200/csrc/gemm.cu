@@ -433,16 +433,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
       k = chunk * 4 + k_in;
       return ((static_cast<uint32_t>(chunk) * kTcN + n) << 4) + (k_in << 2);
     };
+    // A moves in 16-byte chunks (four k values of one row) when every row of
+    // the sector starts on a 16-byte boundary; a thread copies and splits the
+    // same chunks.  A warp's chunks are 8 rows x 4 chunks.
+    const bool a_vector = (t.k & 3) == 0 && (t.a & 3) == 0 && (reinterpret_cast<uintptr_t>(left) & 15) == 0;
+    auto a_chunk = [&](int e, int& m, int& c) -> uint32_t {
+      const int l = e & 31, w = e >> 5;
+      m = (w & 15) * 8 + (l & 7);
+      c = (w >> 4) * 4 + (l >> 3);
+      return (static_cast<uint32_t>(c) * kTcM + m) << 4;
+    };
     auto issue = [&](int64_t s) {
       const uint32_t a_hi = smem + static_cast<uint32_t>(s & 1) * kTcStageBytes;
       const uint32_t b_hi = a_hi + 2 * kTcABytes;
       const int64_t k0 = s * kTcK;
-      for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
-        int m, k;
-        const uint32_t off = a_position(e, m, k);
-        const int64_t row = t.m0 + m, col = k0 + k;
-        const bool valid = row < t.m && col < t.k;
-        TcCopy4(a_hi + off, valid ? left + t.a + row * t.k + col : left, valid);
+      if (a_vector) {
+        for (int e = tid; e < kTcM * kTcK / 4; e += kTcThreads) {
+          int m, c;
+          const uint32_t off = a_chunk(e, m, c);
+          const int64_t row = t.m0 + m, col = k0 + 4 * c;
+          if (row < t.m && col + 4 <= t.k) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a_hi + off), "l"(left + t.a + row * t.k + col)
+                         : "memory");
+          } else {
+            for (int j = 0; j < 4; ++j) {
+              const bool valid = row < t.m && col + j < t.k;
+              TcCopy4(a_hi + off + 4 * j, valid ? left + t.a + row * t.k + col + j : left, valid);
+            }
+          }
+        }
+      } else {
+        for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
+          int m, k;
+          const uint32_t off = a_position(e, m, k);
+          const int64_t row = t.m0 + m, col = k0 + k;
+          const bool valid = row < t.m && col < t.k;
+          TcCopy4(a_hi + off, valid ? left + t.a + row * t.k + col : left, valid);
+        }
       }
       for (int e = tid; e < kTcN * kTcK; e += kTcThreads) {
         int n, k;
@@ -456,14 +483,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
     auto split = [&](int64_t s) {
       const uint32_t a_hi = smem + static_cast<uint32_t>(s & 1) * kTcStageBytes;
       const uint32_t a_lo = a_hi + kTcABytes, b_hi = a_lo + kTcABytes, b_lo = b_hi + kTcBBytes;
-      for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
-        int m, k;
-        const uint32_t off = a_position(e, m, k);
-        float x;
-        asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(a_hi + off));
-        const uint32_t hi = Tf32(x), lo = Tf32(x - __uint_as_float(hi));
-        asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_hi + off), "r"(hi));
-        asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_lo + off), "r"(lo));
+      if (a_vector) {
+        for (int e = tid; e < kTcM * kTcK / 4; e += kTcThreads) {
+          int m, c;
+          const uint32_t off = a_chunk(e, m, c);
+          float x[4];
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(x[0]), "=f"(x[1]), "=f"(x[2]), "=f"(x[3]) : "r"(a_hi + off));
+          uint32_t hi[4], lo[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            hi[j] = Tf32(x[j]);
+            lo[j] = Tf32(x[j] - __uint_as_float(hi[j]));
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" :: "r"(a_hi + off), "r"(hi[0]), "r"(hi[1]), "r"(hi[2]),
+                       "r"(hi[3]));
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" :: "r"(a_lo + off), "r"(lo[0]), "r"(lo[1]), "r"(lo[2]),
+                       "r"(lo[3]));
+        }
+      } else {
+        for (int e = tid; e < kTcM * kTcK; e += kTcThreads) {
+          int m, k;
+          const uint32_t off = a_position(e, m, k);
+          float x;
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(a_hi + off));
+          const uint32_t hi = Tf32(x), lo = Tf32(x - __uint_as_float(hi));
+          asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_hi + off), "r"(hi));
+          asm volatile("st.shared.b32 [%0], %1;" :: "r"(a_lo + off), "r"(lo));
+        }
       }
       for (int e = tid; e < kTcN * kTcK; e += kTcThreads) {
         int n, k;
