@@ -7,10 +7,10 @@
 //
 // F64 and C128 use the FP64 tensor-core MMA (mma.sync m8n8k4 f64, "DMMA");
 // C128 uses four real products per complex product; operands are staged with
-// cp.async (zero-filled at edges) in two stages.  F32 uses the 5th-generation
-// tensor cores (tcgen05.mma kind::tf32, accumulators in tensor memory) with a
-// three-term TF32 split, each 32-deep slice of K summed in FP32 registers
-// (TcGemm).  C64 uses FP32 FMA.
+// cp.async (zero-filled at edges) in two stages.  F32 and C64 use the
+// 5th-generation tensor cores (tcgen05.mma kind::tf32, accumulators in tensor
+// memory) with a three-term TF32 split, each K slice summed in FP32 registers
+// (TcGemm, TcGemmComplex).
 #include "gemm.h"
 
 #include "engine.h"
@@ -44,11 +44,6 @@ __device__ __forceinline__ void CpAsync16(void* smem, const void* gmem, bool val
   const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
   const int bytes = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(gmem), "r"(bytes));
-}
-__device__ __forceinline__ void CpAsync4(void* smem, const void* gmem, bool valid) {
-  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
-  const int bytes = valid ? 4 : 0;
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(gmem), "r"(bytes));
 }
 __device__ __forceinline__ void CpCommit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
@@ -203,72 +198,6 @@ __global__ void __launch_bounds__(kGemmThreads) DmmaGemm(const int64_t* __restri
             out[at] = acc[f][g][j];
           }
         }
-      }
-    }
-  }
-}
-
-// ---------------------------------------------------------------------------
-// FP32 / complex64: each thread owns a 4x4 block of the 64x64 tile.
-template <bool kComplex>
-__global__ void __launch_bounds__(kGemmThreads) FmaGemm(const int64_t* __restrict__ table, int64_t sectors,
-                                                        int64_t tiles, const float* __restrict__ left,
-                                                        const float* __restrict__ right, float* out) {
-  constexpr int BK = 16;
-  constexpr int W = kComplex ? 2 : 1;
-  __shared__ __align__(16) float As[BK][kTile * W + 4];
-  __shared__ __align__(16) float Bs[BK][kTile * W + 4];
-  const int tid = threadIdx.x;
-  const int tr = tid >> 4, tc = tid & 15;
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const Task t = DecodeTask(table, sectors, tile);
-    float acc[4][4][W] = {};
-    for (int64_t k0 = 0; k0 < t.k; k0 += BK) {
-      for (int e = tid; e < kTile * BK; e += kGemmThreads) {    // A transposed into As[k][m]
-        const int r = e / BK, c = e % BK;
-        const bool ok = t.m0 + r < t.m && k0 + c < t.k;
-        for (int w = 0; w < W; ++w)
-          As[c][r * W + w] = ok ? left[W * (t.a + (t.m0 + r) * t.k + k0 + c) + w] : 0.0f;
-      }
-      for (int e = tid; e < kTile * BK; e += kGemmThreads) {
-        const int r = e / kTile, c = e % kTile;
-        const bool ok = k0 + r < t.k && t.n0 + c < t.n;
-        for (int w = 0; w < W; ++w)
-          Bs[r][c * W + w] = ok ? right[W * (t.b + (k0 + r) * t.n + t.n0 + c) + w] : 0.0f;
-      }
-      __syncthreads();
-#pragma unroll 4
-      for (int kk = 0; kk < BK; ++kk) {
-        float a[4][W], b[4][W];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int w = 0; w < W; ++w) { a[i][w] = As[kk][(tr * 4 + i) * W + w]; b[i][w] = Bs[kk][(tc * 4 + i) * W + w]; }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if constexpr (kComplex) {
-              acc[i][j][0] = __fmaf_rn(a[i][0], b[j][0], acc[i][j][0]);
-              acc[i][j][0] = __fmaf_rn(-a[i][1], b[j][1], acc[i][j][0]);
-              acc[i][j][1] = __fmaf_rn(a[i][0], b[j][1], acc[i][j][1]);
-              acc[i][j][1] = __fmaf_rn(a[i][1], b[j][0], acc[i][j][1]);
-            } else {
-              acc[i][j][0] = __fmaf_rn(a[i][0], b[j][0], acc[i][j][0]);
-            }
-          }
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t row = t.m0 + tr * 4 + i;
-      if (row >= t.m) continue;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t col = t.n0 + tc * 4 + j;
-        if (col >= t.n) continue;
-        for (int w = 0; w < W; ++w) out[W * (t.c + row * t.n + col) + w] = acc[i][j][w];
       }
     }
   }
@@ -587,6 +516,270 @@ __global__ void __launch_bounds__(kTcThreads, 1) TcGemm(const int64_t* __restric
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(kTcTmemColumns));
 }
 
+// ---------------------------------------------------------------------------
+// Complex64 on tcgen05: the same pipeline as TcGemm with real and imaginary
+// planes.  Per 8-deep step, Cr += Ar Br - Ai Bi and Ci += Ar Bi + Ai Br, each
+// product as three TF32 terms (the minus by the instruction descriptor's A
+// negate bit): 12 MMAs into two accumulators (re, im) per buffer.  A slice is
+// 16 deep so that a stage (four A planes of 128 x 16, four B planes of
+// 64 x 16) stays 48 KB.  Raw interleaved values land in the lo planes and the
+// copying thread splits them into the four planes.
+constexpr int kTcKc = 16;
+constexpr uint32_t kTcAPlane = kTcM * kTcKc * 4;   // 8 KB
+constexpr uint32_t kTcBPlane = kTcN * kTcKc * 4;   // 4 KB
+static_assert(4 * kTcAPlane + 4 * kTcBPlane == kTcStageBytes, "complex stage must match the real stage size");
+constexpr uint32_t kTcTmemColumnsComplex = 4 * kTcN;   // two buffers of (re, im)
+
+__global__ void __launch_bounds__(kTcThreads, 2) TcGemmComplex(const int64_t* __restrict__ table, int64_t sectors,
+                                                              int64_t tiles, const float* __restrict__ left,
+                                                              const float* __restrict__ right, float* out) {
+  extern __shared__ __align__(1024) unsigned char tc_smem[];
+  __shared__ __align__(8) uint64_t mbar_storage[2];
+  __shared__ uint32_t tmem_slot;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const uint32_t smem = static_cast<uint32_t>(__cvta_generic_to_shared(tc_smem));
+  const uint32_t mbar0 = static_cast<uint32_t>(__cvta_generic_to_shared(&mbar_storage[0]));
+  if (warp == 0) {
+    const uint32_t slot = static_cast<uint32_t>(__cvta_generic_to_shared(&tmem_slot));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" :: "r"(slot),
+                 "r"(kTcTmemColumnsComplex));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(mbar0));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" :: "r"(mbar0 + 8));
+    asm volatile("fence.mbarrier_init.release.cluster;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem = tmem_slot;
+  // kind::tf32, F32 accumulate, A and B K-major, N = 64, M = 128; bit 13 negates A.
+  const uint32_t idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kTcN >> 3) << 17) | ((kTcM >> 4) << 24);
+  const uint32_t idesc_negate = idesc | (1u << 13);
+  uint32_t parity[2] = {0, 0};
+  bool ok = true;
+  // Planes of stage s: A re hi, re lo, im hi, im lo, then B in the same order.
+  auto plane_a = [&](int64_t s, int p) { return smem + static_cast<uint32_t>(s & 1) * kTcStageBytes + p * kTcAPlane; };
+  auto plane_b = [&](int64_t s, int p) {
+    return smem + static_cast<uint32_t>(s & 1) * kTcStageBytes + 4 * kTcAPlane + p * kTcBPlane;
+  };
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const TcTask t = DecodeTcTask(table, sectors, tile);
+    float acc_re[32], acc_im[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc_re[j] = acc_im[j] = 0.0f;
+    const int64_t slices = (t.k + kTcKc - 1) / kTcKc;
+    auto drain = [&](int64_t s) {
+      const int buf = static_cast<int>(s & 1);
+      ok = WaitPhase(mbar0 + 8 * buf, parity[buf]) && ok;
+      parity[buf] ^= 1u;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
+      float v[32];
+      TmemLoad32(tmem + lanes + static_cast<uint32_t>(buf * 2 * kTcN + half * 32), v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc_re[j] = __fadd_rn(acc_re[j], v[j]);
+      TmemLoad32(tmem + lanes + static_cast<uint32_t>(buf * 2 * kTcN + kTcN + half * 32), v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc_im[j] = __fadd_rn(acc_im[j], v[j]);
+    };
+    auto a_position = [&](int e, int& m, int& k) -> uint32_t {
+      const int k_in = e & 3, m_lo = (e >> 2) & 7, chunk = (e >> 5) & 3, m_hi = e >> 7;
+      m = m_hi * 8 + m_lo;
+      k = chunk * 4 + k_in;
+      return ((static_cast<uint32_t>(chunk) * kTcM + m) << 4) + (k_in << 2);
+    };
+    auto a_chunk = [&](int e, int& m, int& c) -> uint32_t {
+      const int l = e & 31, w = e >> 5;
+      m = w * 8 + (l & 7);
+      c = l >> 3;
+      return (static_cast<uint32_t>(c) * kTcM + m) << 4;
+    };
+    auto b_position = [&](int e, int& n, int& k) -> uint32_t {
+      const int l = e & 31, w = e >> 5;
+      const int k_in = l >> 3, chunk = w >> 3;
+      n = (w & 7) * 8 + (l & 7);
+      k = chunk * 4 + k_in;
+      return ((static_cast<uint32_t>(chunk) * kTcN + n) << 4) + (k_in << 2);
+    };
+    // A moves as 32-byte chunks (four complex values of one row: two 16-byte
+    // copies, parked interleaved in the two lo planes) when its rows start on
+    // 16-byte boundaries; otherwise, and at the K edge, value by value into
+    // the lo planes as re / im.
+    const bool a_vector = (t.k & 1) == 0 && (t.a & 1) == 0 && (reinterpret_cast<uintptr_t>(left) & 15) == 0;
+    auto whole_chunk = [&](int64_t row, int64_t col) { return row < t.m && col + 4 <= t.k; };
+    auto issue = [&](int64_t s) {
+      const uint32_t are_lo = plane_a(s, 1), aim_lo = plane_a(s, 3);
+      const uint32_t bre_lo = plane_b(s, 1), bim_lo = plane_b(s, 3);
+      const int64_t k0 = s * kTcKc;
+      if (a_vector) {
+        for (int e = tid; e < kTcM * kTcKc / 4; e += kTcThreads) {
+          int m, c;
+          const uint32_t off = a_chunk(e, m, c);
+          const int64_t row = t.m0 + m, col = k0 + 4 * c;
+          if (whole_chunk(row, col)) {
+            const float* src = left + 2 * (t.a + row * t.k + col);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(are_lo + off), "l"(src) : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(aim_lo + off), "l"(src + 4) : "memory");
+          } else {
+            for (int j = 0; j < 4; ++j) {
+              const bool valid = row < t.m && col + j < t.k;
+              const float* src = valid ? left + 2 * (t.a + row * t.k + col + j) : left;
+              TcCopy4(are_lo + off + 4 * j, src, valid);
+              TcCopy4(aim_lo + off + 4 * j, valid ? src + 1 : left, valid);
+            }
+          }
+        }
+      } else {
+        for (int e = tid; e < kTcM * kTcKc; e += kTcThreads) {
+          int m, k;
+          const uint32_t off = a_position(e, m, k);
+          const int64_t row = t.m0 + m, col = k0 + k;
+          const bool valid = row < t.m && col < t.k;
+          const float* src = valid ? left + 2 * (t.a + row * t.k + col) : left;
+          TcCopy4(are_lo + off, src, valid);
+          TcCopy4(aim_lo + off, valid ? src + 1 : left, valid);
+        }
+      }
+      for (int e = tid; e < kTcN * kTcKc; e += kTcThreads) {
+        int n, k;
+        const uint32_t off = b_position(e, n, k);
+        const int64_t row = k0 + k, col = t.n0 + n;
+        const bool valid = row < t.k && col < t.n;
+        const float* src = valid ? right + 2 * (t.b + row * t.n + col) : right;
+        TcCopy4(bre_lo + off, src, valid);
+        TcCopy4(bim_lo + off, valid ? src + 1 : right, valid);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // Split one complex value (read from the raw lo planes by the caller)
+    // into the four planes at one 4-byte position.
+    auto put = [&](uint32_t re_hi, uint32_t re_lo, uint32_t im_hi, uint32_t im_lo, uint32_t off, float re, float im) {
+      const uint32_t rh = Tf32(re), rl = Tf32(re - __uint_as_float(rh));
+      const uint32_t ih = Tf32(im), il = Tf32(im - __uint_as_float(ih));
+      asm volatile("st.shared.b32 [%0], %1;" :: "r"(re_hi + off), "r"(rh));
+      asm volatile("st.shared.b32 [%0], %1;" :: "r"(re_lo + off), "r"(rl));
+      asm volatile("st.shared.b32 [%0], %1;" :: "r"(im_hi + off), "r"(ih));
+      asm volatile("st.shared.b32 [%0], %1;" :: "r"(im_lo + off), "r"(il));
+    };
+    auto ld = [](uint32_t address) {
+      float x;
+      asm volatile("ld.shared.f32 %0, [%1];" : "=f"(x) : "r"(address));
+      return x;
+    };
+    auto split = [&](int64_t s) {
+      const uint32_t are_hi = plane_a(s, 0), are_lo = plane_a(s, 1), aim_hi = plane_a(s, 2), aim_lo = plane_a(s, 3);
+      const uint32_t bre_hi = plane_b(s, 0), bre_lo = plane_b(s, 1), bim_hi = plane_b(s, 2), bim_lo = plane_b(s, 3);
+      const int64_t k0 = s * kTcKc;
+      if (a_vector) {
+        for (int e = tid; e < kTcM * kTcKc / 4; e += kTcThreads) {
+          int m, c;
+          const uint32_t off = a_chunk(e, m, c);
+          float re[4], im[4];
+          if (whole_chunk(t.m0 + m, k0 + 4 * c)) {
+            // Raw interleaved: (re0 im0 re1 im1) in the re lo plane, (re2 im2 re3 im3) in the im lo plane.
+            re[0] = ld(are_lo + off); im[0] = ld(are_lo + off + 4); re[1] = ld(are_lo + off + 8); im[1] = ld(are_lo + off + 12);
+            re[2] = ld(aim_lo + off); im[2] = ld(aim_lo + off + 4); re[3] = ld(aim_lo + off + 8); im[3] = ld(aim_lo + off + 12);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              re[j] = ld(are_lo + off + 4 * j);
+              im[j] = ld(aim_lo + off + 4 * j);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) put(are_hi, are_lo, aim_hi, aim_lo, off + 4 * j, re[j], im[j]);
+        }
+      } else {
+        for (int e = tid; e < kTcM * kTcKc; e += kTcThreads) {
+          int m, k;
+          const uint32_t off = a_position(e, m, k);
+          put(are_hi, are_lo, aim_hi, aim_lo, off, ld(are_lo + off), ld(aim_lo + off));
+        }
+      }
+      for (int e = tid; e < kTcN * kTcKc; e += kTcThreads) {
+        int n, k;
+        const uint32_t off = b_position(e, n, k);
+        put(bre_hi, bre_lo, bim_hi, bim_lo, off, ld(bre_lo + off), ld(bim_lo + off));
+      }
+    };
+    if (slices > 0) issue(0);
+    for (int64_t s = 0; s < slices; ++s) {
+      const int buf = static_cast<int>(s & 1);
+      if (s > 0) drain(s - 1);
+      if (s + 1 < slices) {
+        issue(s + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      split(s);
+      asm volatile("fence.proxy.async.shared::cta;");
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncthreads();
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      if (tid == 0) {
+        const uint32_t d_re = tmem + static_cast<uint32_t>(buf * 2 * kTcN), d_im = d_re + kTcN;
+#pragma unroll
+        for (int step = 0; step < kTcKc / 8; ++step) {
+          const uint32_t a_step = static_cast<uint32_t>(step) * 2 * kTcM * 16;
+          const uint32_t b_step = static_cast<uint32_t>(step) * 2 * kTcN * 16;
+          uint64_t a[4], b[4];   // re hi, re lo, im hi, im lo
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            a[p] = SmemDescriptor(plane_a(s, p) + a_step, kTcM * 16, 128);
+            b[p] = SmemDescriptor(plane_b(s, p) + b_step, kTcN * 16, 128);
+          }
+          const uint32_t first = step == 0 ? 0u : 1u;
+          // re: Ar Br - Ai Bi
+          MmaTf32(d_re, a[1], b[0], idesc, first);
+          MmaTf32(d_re, a[0], b[1], idesc, 1u);
+          MmaTf32(d_re, a[0], b[0], idesc, 1u);
+          MmaTf32(d_re, a[3], b[2], idesc_negate, 1u);
+          MmaTf32(d_re, a[2], b[3], idesc_negate, 1u);
+          MmaTf32(d_re, a[2], b[2], idesc_negate, 1u);
+          // im: Ar Bi + Ai Br
+          MmaTf32(d_im, a[1], b[2], idesc, first);
+          MmaTf32(d_im, a[0], b[3], idesc, 1u);
+          MmaTf32(d_im, a[0], b[2], idesc, 1u);
+          MmaTf32(d_im, a[3], b[0], idesc, 1u);
+          MmaTf32(d_im, a[2], b[1], idesc, 1u);
+          MmaTf32(d_im, a[2], b[0], idesc, 1u);
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     :: "r"(mbar0 + 8 * buf) : "memory");
+      }
+    }
+    if (slices > 0) drain(slices - 1);
+    if (!ok) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc_re[j] = acc_im[j] = __int_as_float(0x7fc00000);
+    }
+    const int64_t row = t.m0 + quarter * 32 + lane;
+    if (row < t.m) {
+      float* dst = out + 2 * (t.c + row * t.n + t.n0 + half * 32);
+      const int64_t width = t.n - t.n0 - half * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < width) {
+          dst[2 * j] = acc_re[j];
+          dst[2 * j + 1] = acc_im[j];
+        }
+      }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(kTcTmemColumnsComplex));
+  }
+}
+
 int SmCountGemm() {
   static int count = [] {
     int device = 0, sms = 148;
@@ -709,11 +902,15 @@ void SectorGemm(int32_t dtype, int64_t sectors, const int64_t* host_table, const
           static_cast<float*>(output));
       break;
     }
-    case 15:
-      FmaGemm<true><<<static_cast<unsigned>(grid), kGemmThreads, 0, stream>>>(
-          device_table, sectors, tiles, static_cast<const float*>(left), static_cast<const float*>(right),
+    case 15: {
+      Check(cudaFuncSetAttribute(TcGemmComplex, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem),
+            "tcgen05 GEMM shared memory");
+      const int64_t tc_grid = std::min<int64_t>(tc_tiles, int64_t{SmCountGemm()} * 2);
+      TcGemmComplex<<<static_cast<unsigned>(tc_grid), kTcThreads, kTcSmem, stream>>>(
+          device_table, sectors, tc_tiles, static_cast<const float*>(left), static_cast<const float*>(right),
           static_cast<float*>(output));
       break;
+    }
     default:
       throw InvalidArgument("sector GEMM supports only F32/F64/C64/C128");
   }

@@ -228,23 +228,26 @@ def test_sector_gemm(dtype):
     assert_close(got, so.sector_gemm(np.array(spec), left, right, c_off), dtype)
 
 
-def test_sector_gemm_f32_long_k_on_tensor_cores():
-    """F32 sectors run on tcgen05 (three-term TF32 split, 32-deep K slices
-    summed in FP32 registers): the error stays within the f32 tolerance for
-    K in the thousands, several 128 x 64 tiles per sector and ragged edges."""
+@pytest.mark.parametrize("dtype", [np.float32, np.complex64])
+def test_sector_gemm_single_precision_long_k_on_tensor_cores(dtype):
+    """F32 and C64 sectors run on tcgen05 (three-term TF32 split, K slices
+    summed in FP32 registers; C64 as four real products with A negated for
+    -Ai Bi): the error stays within the single-precision tolerance for K in
+    the thousands, several 128 x 64 tiles per sector and ragged edges."""
     rng = np.random.default_rng(33)
     shapes = [(300, 200, 2048), (129, 65, 1000), (7, 3, 4097)]
     spec, a_off, b_off, c_off = [], 0, 0, 0
     for m, n, k in shapes:
         spec.append((m, n, k, a_off, b_off, c_off))
         a_off, b_off, c_off = a_off + m * k, b_off + k * n, c_off + m * n
-    left, right = sample(rng, np.float32, a_off), sample(rng, np.float32, b_off)
+    left, right = sample(rng, dtype, a_off), sample(rng, dtype, b_off)
+    wide = np.complex128 if dtype == np.complex64 else np.float64
     plan = stride.GemmPlan(np.array(spec))
     for _ in range(2):
-        out = torch.full((c_off,), float("nan"), dtype=torch.float32, device="cuda")
+        out = torch.full((c_off,), float("nan"), dtype=TORCH[dtype], device="cuda")
         got = host(stride.sector_gemm(plan, cuda(left), cuda(right), out))
-        expected = so.sector_gemm(np.array(spec), left.astype(np.float64), right.astype(np.float64), c_off)
-        assert_close(got, expected, np.float32)
+        expected = so.sector_gemm(np.array(spec), left.astype(wide), right.astype(wide), c_off)
+        assert_close(got, expected, dtype)
 
 
 @pytest.mark.parametrize("dtype", [np.float64, np.complex128])
