@@ -263,9 +263,9 @@ int t0b_axpby(int32_t dtype, int64_t n, double alpha_real, double alpha_imag, co
  * must be pairwise disjoint, the output must not overlap either input, and
  * the operands must be aligned to their element size (16 bytes for C128);
  * otherwise status 1 and nothing is launched.  F64 and C128 run on the FP64
- * tensor cores (DMMA); F32 runs on the tcgen05 tensor cores (kind::tf32,
- * three-term split, each 32-deep K slice summed into FP32 registers); C64
- * accumulates in FP32 FMA.
+ * tensor cores (DMMA); F32 and C64 run on the tcgen05 tensor cores
+ * (kind::tf32, three-term split, each K slice summed into FP32 registers;
+ * C64 as four real products).
  */
 size_t t0b_gemm_table_words(int64_t sectors);
 int t0b_gemm_table_build(int64_t sectors, const int64_t* spec, int64_t* table, char* error,
