@@ -112,7 +112,7 @@ typedef struct {
   uint64_t records;
   uint64_t tiles;
   uint64_t kernels_per_call;
-  uint64_t full_coverage;
+  uint64_t full_coverage;     /* 1: every output element is written once, no zeroing pass */
   uint64_t bytes_moved;       /* algorithmic bytes of one batch */
 } t0b_plan_info;
 void t0b_plan_query(const t0b_plan* plan, t0b_plan_info* info);

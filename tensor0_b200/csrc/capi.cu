@@ -166,6 +166,7 @@ void RunReduce(const t0b_plan* plan, int32_t dtype, int32_t ca_dtype, const void
     args.ca = ca;
     args.ca_count = ca_count;
     args.conjugate = plan->plan.conjugate ? 1 : 0;
+    args.assign = plan->plan.reduce_assign ? 1 : 0;
     t0b::LaunchReduce(dtype, ca_dtype, args, stream);
   }
 }

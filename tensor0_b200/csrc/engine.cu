@@ -774,7 +774,7 @@ __global__ void __launch_bounds__(kThreads) ReduceFinish(ReduceArgs args) {
       at += static_cast<int64_t>(rem - next * static_cast<uint32_t>(g.n[a])) * g.d[a];
       rem = next;
     }
-    out[at] = Add(out[at], sum);
+    out[at] = args.assign ? PlusZero(sum) : Add(out[at], sum);
   }
 }
 

@@ -51,6 +51,7 @@ struct ReduceArgs {
   const void* ca;
   int64_t ca_count;
   int conjugate;                    // read conj(source) (complex storage)
+  int assign;                       // pass 2 writes 0 + sum (the output was not zeroed) instead of adding
 };
 
 struct DotArgs {

@@ -888,8 +888,11 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
   plan.tasks = static_cast<uint64_t>(tasks);
   plan.owners = static_cast<uint64_t>(owners);
   plan.scratch = static_cast<uint64_t>(scratch);
-  // Every output element is written by the map engine exactly once.
-  plan.full_coverage = disjoint && !plan.has_reduce && covered == plan.output_size;
+  // Every output element is written by the map engine exactly once, or (a
+  // trace's usual case) the reduce engine's owners cover the output exactly
+  // once in one wave, so pass 2 assigns 0 + sum and no zeroing is needed.
+  plan.reduce_assign = disjoint && plan.has_reduce && !plan.has_map && covered == plan.output_size;
+  plan.full_coverage = (disjoint && !plan.has_reduce && covered == plan.output_size) || plan.reduce_assign;
   const uint64_t out_bytes = plan.output_size * element_bytes;
   plan.bytes_moved = read_elements * element_bytes + out_bytes + (operation == 1 ? out_bytes : 0);
 

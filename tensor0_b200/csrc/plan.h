@@ -195,7 +195,8 @@ struct Plan {
   uint64_t output_size = 0;
   uint64_t records = 0;
   uint64_t coefficient_rows = 0;
-  bool full_coverage = false;    // the map engine writes every output element
+  bool full_coverage = false;    // every output element is written exactly once (no zeroing first)
+  bool reduce_assign = false;    // the reduce engine's owners alone cover the output once: pass 2 assigns
   bool has_map = false;
   bool has_reduce = false;
   bool map_wide = false;         // some tile needs 64-bit in-tile offsets
