@@ -190,6 +190,23 @@ def test_sector_gemm_validates_operands_before_any_launch(lib):
     assert lib.t0b_kernel_launches() == launches
 
 
+def test_gemm_table_carries_both_tile_prefixes(lib):
+    """Row 6 counts 64 x 64 tiles (DMMA), row 7 128 x 64 tiles (tcgen05); a
+    table whose prefixes disagree with its sizes is rejected before launch."""
+    spec = np.array([[70, 33, 129, 0, 0, 0], [300, 200, 8, 0, 0, 2310], [0, 4, 3, 0, 0, 62310]])
+    plan = stride.GemmPlan(spec)
+    rows = plan.table.reshape(-1, 8)
+    assert list(rows[:, 6]) == [0, 2, 2 + 5 * 4]
+    assert list(rows[:, 7]) == [0, 1, 1 + 3 * 4]
+    tampered = plan.table.copy()
+    tampered[8 + 7] += 1
+    err = _native.error_buffer()
+    status = lib.t0b_sector_gemm(_native.F32, plan.sectors, tampered.ctypes.data_as(_native.c_i64p),
+                                 ctypes.c_void_p(0x90000), ctypes.c_void_p(0x1000), 1 << 20, ctypes.c_void_p(0x400000),
+                                 1 << 20, ctypes.c_void_p(0x800000), 1 << 20, None, err, len(err))
+    assert status == 1 and b"tile prefix is inconsistent" in err.value
+
+
 def test_disjointness_is_proven_for_large_packed_permutes(lib):
     """Without the producer's assertion the planner proves the full-size U(1)
     4-leg permute disjoint (1.02e9 outputs, beyond a bitmap's reach) by the
