@@ -395,6 +395,7 @@ def execute_grouped(source: torch.Tensor, plan: Plan, matrices: torch.Tensor, *,
 
 
 _GROUPED_PLANS: dict[tuple[bytes, int], Plan] = {}
+_GROUPED_MATRICES: dict[tuple, torch.Tensor] = {}
 
 
 def grouped_transform(source: torch.Tensor, source_layout, destination_layout, result_dtype, permutation,
@@ -422,7 +423,15 @@ def grouped_transform(source: torch.Tensor, source_layout, destination_layout, r
         flat = flat.astype(np.complex64 if single else np.complex128)
     else:
         flat = np.real(flat).astype(np.float32 if single else np.float64)
-    device_matrices = torch.from_numpy(np.ascontiguousarray(flat)).to(source.device)
+    # The basis matrices of a call site repeat from call to call: keep them on
+    # the device (keyed by their bytes) instead of copying them every call.
+    matrix_key = (key, str(source.device), flat.dtype.str, flat.tobytes())
+    device_matrices = _GROUPED_MATRICES.get(matrix_key)
+    if device_matrices is None:
+        device_matrices = torch.from_numpy(np.ascontiguousarray(flat)).to(source.device)
+        if len(_GROUPED_MATRICES) > 256:
+            _GROUPED_MATRICES.clear()
+        _GROUPED_MATRICES[matrix_key] = device_matrices
     return execute_grouped(source, plan, device_matrices)
 
 
