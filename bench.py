@@ -393,18 +393,20 @@ def grouped_bench(device, steps: int, warmup: int, extent: int = 16):
                          "algorithmic_bytes_per_launch": algorithmic}}
 
 
-def gemm_f32_bench(device, steps: int, warmup: int, size: int = 4096):
-    """One f32 sector of size^3 through the tcgen05 GEMM (three-term TF32
-    split, FP32 register accumulation per 32-deep slice) beside cuBLAS FP32
-    (TF32 off) on the same operands; TFLOP/s at 2 size^3 per call."""
+def gemm_f32_bench(device, steps: int, warmup: int, size: int = 4096, dtype: str = "f32"):
+    """One single-precision sector of size^3 through the tcgen05 GEMM
+    (three-term TF32 split, FP32 register accumulation per K slice; c64 as four
+    real products) beside cuBLAS (TF32 off) on the same operands; TFLOP/s at
+    2 size^3 (f32) or 8 size^3 (c64) per call."""
     import torch
     from tensor0_b200 import stride
+    tdtype = torch.complex64 if dtype == "c64" else torch.float32
     plan = stride.GemmPlan(np.array([(size, size, size, 0, 0, 0)]))
     gen = torch.Generator(device=device)
     gen.manual_seed(11)
-    left = torch.randn(size * size, generator=gen, device=device)
-    right = torch.randn(size * size, generator=gen, device=device)
-    out = torch.empty(size * size, device=device)
+    left = torch.randn(size * size, generator=gen, device=device, dtype=tdtype)
+    right = torch.randn(size * size, generator=gen, device=device, dtype=tdtype)
+    out = torch.empty(size * size, device=device, dtype=tdtype)
     stream = torch.cuda.current_stream(device)
     for _ in range(warmup):
         stride.sector_gemm(plan, left, right, out)
@@ -416,13 +418,16 @@ def gemm_f32_bench(device, steps: int, warmup: int, size: int = 4096):
         torch.matmul(a, b)
     reference, _ = timed_events(stream, steps, lambda _: torch.matmul(a, b))
     torch.backends.cuda.matmul.allow_tf32 = previous
-    flops = 2.0 * size ** 3
-    error = float((out.view(size, size).double() - a.double() @ b.double()).abs().max()
-                  / (a.double() @ b.double()).abs().max())
-    return {"metric": "f32 sector GEMM TFLOP/s", "kernel": "TcGemm (tcgen05.mma kind::tf32, 3 terms)",
+    flops = (8.0 if dtype == "c64" else 2.0) * size ** 3
+    wide = torch.complex128 if dtype == "c64" else torch.float64
+    exact = a.to(wide) @ b.to(wide)
+    error = float((out.view(size, size).to(wide) - exact).abs().max() / exact.abs().max())
+    kernel = "TcGemmComplex (tcgen05.mma kind::tf32, 4 products x 3 terms)" if dtype == "c64" else \
+        "TcGemm (tcgen05.mma kind::tf32, 3 terms)"
+    return {"metric": f"{dtype} sector GEMM TFLOP/s", "kernel": kernel,
             "shape": f"{size}^3", "ms_per_call": round(total / steps, 4),
             "value": round(flops / (total / steps / 1e3) / 1e12, 2), "unit": "TFLOP/s",
-            "cublas_fp32": round(flops / (reference / steps / 1e3) / 1e12, 2), "max_relative_error": error}
+            "cublas": round(flops / (reference / steps / 1e3) / 1e12, 2), "max_relative_error": error}
 
 
 def device_uuid(index: int) -> str:
@@ -755,9 +760,10 @@ def main():
         trace = trace_bench(device, max(args.steps, 5), args.warmup,
                             tuple(int(d) for d in args.trace_degeneracies.split(",")))
 
-    gemm_f32 = None
+    gemm_f32 = gemm_c64 = None
     if not args.no_contraction:
         gemm_f32 = gemm_f32_bench(device, max(args.steps, 5), args.warmup)
+        gemm_c64 = gemm_f32_bench(device, max(args.steps, 5), args.warmup, size=2048, dtype="c64")
 
     grouped = None
     if not args.no_grouped:
@@ -790,6 +796,7 @@ def main():
         "trace": trace,
         "grouped": grouped,
         "gemm_f32": gemm_f32,
+        "gemm_c64": gemm_c64,
     }
     print(json.dumps(line), flush=True)
 
