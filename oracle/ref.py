@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -40,6 +41,12 @@ def build(reference: str | None = None) -> Path:
     if not Path(reference).exists():
         raise RuntimeError("reference sources are not present; oracle/_ref cannot be rebuilt here")
     subprocess.run(["make", "-C", str(HERE), f"REFERENCE={reference}", f"-j{os.cpu_count() or 4}"], check=True)
+    # The reference's CUDA companion for sm_100a (a same-GPU reference for the
+    # tests); a toolchain that cannot build it leaves those tests skipped.
+    companion = subprocess.run(["make", "-C", str(HERE), "cuda", f"REFERENCE={reference}",
+                                f"-j{os.cpu_count() or 4}"])
+    if companion.returncode != 0:
+        print("oracle: the reference's CUDA companion did not build; its tests will skip", file=sys.stderr)
     return LIBRARY
 
 

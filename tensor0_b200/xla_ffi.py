@@ -80,7 +80,16 @@ def registration() -> dict[str, int]:
     """Addresses keyed as the reference's ``_stride_cuda_registration()`` dict:
     ``{op}_instantiate``, ``{op}_{f32,f64,c64,c128}``, ``{op}_type_id`` and
     ``{op}_type_info``."""
-    lib = library()
+    return registration_of(library())
+
+
+def registration_of(lib: ctypes.CDLL) -> dict[str, int]:
+    """The same addresses from any library exporting the symbol table (the
+    reference's own companion too)."""
+    for name in handler_symbols():
+        function = getattr(lib, name)
+        function.argtypes = []
+        function.restype = ctypes.c_uint64 if name.endswith("Count") else ctypes.c_void_p
     table = {}
     for operation in OPERATIONS:
         stem = "Tensor0StrideCuda" + _capitalized(operation)

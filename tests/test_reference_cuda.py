@@ -1,0 +1,252 @@
+"""The reference's own CUDA companion as a same-GPU reference.
+
+``make -C oracle cuda`` builds crates/tensor0-cuda12/native/cuda/*.cu (with
+the layout decoder it links) for sm_100a into oracle/_ref/libt0ref_cuda.so.
+Its 45 XLA FFI symbols are the table this library's handler library exports
+(crates/tensor0-py/src/stride.rs:284-330), so the same ctypes XLA host drives
+both.  Call sites are assembled as the reference's lowering does
+(src/tensor0/_stride/_ffi/_calls.py:229-293): the layout attribute is the
+prepared words (Tensor0StridePrepareLayout), the reference's descriptor
+operand its packed owner/fiber words (Tensor0StridePackOwnerFiber,
+descriptor.cc:407-440), its accumulation scratch sized by
+Tensor0StrideSumScratchCapacity; this library gets its own packed table.
+
+CPU: the companion exports the table and packs descriptors.  GPU: on the same
+inputs, this library's copy, update and accumulation handlers reproduce the
+companion's results bit for bit, on random layouts and on the U(1) four-leg
+permute workload, whose device time per call is printed for both.
+"""
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from random_layouts import random_layout
+from tensor0_b200 import _native, build, stride, xla_ffi
+from xla_host import Host
+
+LIBRARY = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libt0ref_cuda.so"
+if not LIBRARY.is_file():
+    pytest.skip("the reference's CUDA companion is not built (make -C oracle cuda)", allow_module_level=True)
+if not xla_ffi.library_path().exists() and build.xla_ffi_include() is None:
+    pytest.skip("XLA FFI headers absent: the handler library is not built", allow_module_level=True)
+
+OPERATIONS = {"copy": 0, "update": 1, "dot": 2, "accumulation": 3, "reduction": 4}
+SUFFIX = {np.float32: "f32", np.float64: "f64", np.complex64: "c64", np.complex128: "c128"}
+DTYPES = list(SUFFIX)
+_RECEIVE = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64), ctypes.c_size_t,
+                            ctypes.c_char_p, ctypes.c_size_t)
+
+
+@pytest.fixture(scope="module")
+def companion():
+    import torch  # noqa: F401  (the companion forwards to the resident libcudart.so.12 torch loads)
+    lib = ctypes.CDLL(str(LIBRARY))
+    for name in ("Tensor0StridePrepareLayout", "Tensor0StridePackOwnerFiber", "Tensor0StrideSumScratchCapacity"):
+        function = getattr(lib, name)
+        function.argtypes = [ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, _RECEIVE]
+        function.restype = None
+    return lib
+
+
+@pytest.fixture(scope="module")
+def hosts(companion):
+    build.build_xla()
+    return Host(companion, xla_ffi.registration_of(companion)), Host(xla_ffi.library(), xla_ffi.registration())
+
+
+def native_words(lib, entry: str, operation: str, words) -> np.ndarray:
+    """One of the companion's layout entry points, called as stride.rs:632-700 does."""
+    result = {}
+
+    def receive(context, status, data, count, message, length):
+        result["status"] = status
+        result["words"] = np.array([data[i] for i in range(count)], np.int64)
+        result["message"] = ctypes.string_at(message, length).decode() if length else ""
+
+    callback = _RECEIVE(receive)
+    words = np.ascontiguousarray(words, np.int64)
+    getattr(lib, entry)(OPERATIONS[operation], words.ctypes.data, len(words), None, callback)
+    if result.get("status") != 0:
+        raise ValueError(result.get("message", "no result"))
+    return result["words"]
+
+
+def test_companion_exports_the_handler_table(companion):
+    table = xla_ffi.registration_of(companion)
+    assert len(table) == 35 and all(table.values())
+    assert table != xla_ffi.registration()   # a separate library, not this one resolved twice
+
+
+def test_companion_packs_and_rejects_layouts(companion):
+    records = random_layout(np.random.default_rng(3), 600, 800, 12)
+    words = stride.encode_layout(records, source_size=600, output_size=800)
+    prepared = native_words(companion, "Tensor0StridePrepareLayout", "copy", words)
+    packed = native_words(companion, "Tensor0StridePackOwnerFiber", "copy", prepared)
+    assert len(packed) > 0
+    capacity = native_words(companion, "Tensor0StrideSumScratchCapacity", "accumulation", prepared)
+    assert capacity.shape == (1,) and capacity[0] >= 0
+    with pytest.raises(ValueError):
+        native_words(companion, "Tensor0StridePackOwnerFiber", "copy", prepared[:-1])
+
+
+# ---------------------------------------------------------------------------
+# GPU: this library against the companion on the same inputs.
+
+def _torch():
+    import torch
+    return torch
+
+
+def cuda(array):
+    return _torch().from_numpy(np.ascontiguousarray(array)).cuda()
+
+
+def bits(tensor):
+    _torch().cuda.synchronize()
+    return np.ascontiguousarray(tensor.cpu().numpy()).view(np.uint8)
+
+
+def sample(rng, dtype, shape):
+    if np.iscomplexobj(np.zeros(1, dtype)):
+        return (rng.standard_normal(shape) + 1j * rng.standard_normal(shape)).astype(dtype)
+    return rng.standard_normal(shape).astype(dtype)
+
+
+class Site:
+    """One call site on both libraries: instantiate, execute, destroy."""
+
+    def __init__(self, hosts, companion, operation, words, dtype, coefficient_records=None):
+        self.reference, self.ours = hosts
+        self.operation, self.dtype = operation, dtype
+        self.words = native_words(companion, "Tensor0StridePrepareLayout", operation, words)
+        attrs = {} if coefficient_records is None else {"coefficient_records": list(coefficient_records)}
+        self.contexts = (self.reference.instantiate(operation, layout=list(self.words), **attrs),
+                         self.ours.instantiate(operation, layout=list(self.words), **attrs))
+        self.tables = (cuda(native_words(companion, "Tensor0StridePackOwnerFiber", operation, self.words)),
+                       cuda(xla_ffi.descriptor(operation, self.words, dtype,
+                                               coefficient_records=coefficient_records or ())))
+        self.capacity = (int(native_words(companion, "Tensor0StrideSumScratchCapacity", operation, self.words)[0])
+                         if operation == "accumulation" else 0)
+
+    def call(self, side, args, rets):
+        host = (self.reference, self.ours)[side]
+        host.execute(self.operation, SUFFIX[self.dtype], self.contexts[side], args(self.tables[side]), rets)
+
+    def close(self):
+        self.reference.destroy(self.operation, self.contexts[0])
+        self.ours.destroy(self.operation, self.contexts[1])
+
+
+def scratch_for(site, side, batches, plan_elements):
+    elements = site.capacity if side == 0 else plan_elements
+    return _torch().zeros((batches, elements), dtype=_torch_dtype(site.dtype), device="cuda")
+
+
+def _torch_dtype(dtype):
+    torch = _torch()
+    return {np.float32: torch.float32, np.float64: torch.float64, np.complex64: torch.complex64,
+            np.complex128: torch.complex128}[dtype]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_handlers_match_the_reference_companion_bit_for_bit(hosts, companion, dtype):
+    torch = _torch()
+    rng = np.random.default_rng(41)
+    records = random_layout(rng, 600, 800, 12)
+    words = stride.encode_layout(records, source_size=600, output_size=800)
+    x, base = cuda(sample(rng, dtype, (3, 600))), cuda(sample(rng, dtype, (3, 800)))
+    real = np.float32 if dtype in (np.float32, np.complex64) else np.float64
+    zeros = lambda: torch.zeros((3, 800), dtype=_torch_dtype(dtype), device="cuda")  # noqa: E731
+
+    site = Site(hosts, companion, "copy", words, dtype)
+    outs = [zeros(), zeros()]
+    for side in (0, 1):
+        site.call(side, lambda table: [x, table], [outs[side]])
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    site.close()
+
+    site = Site(hosts, companion, "update", words, dtype)
+    alpha, beta = cuda(np.array(-2.0, real)), cuda(np.array([0.5, 0.0, 1.0], real))
+    outs = [zeros(), zeros()]
+    for side in (0, 1):
+        site.call(side, lambda table: [x, base, alpha, beta, table], [outs[side]])
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    site.close()
+
+    selected = [0, 2, 5, 7]
+    site = Site(hosts, companion, "accumulation", words, dtype, coefficient_records=selected)
+    plan = stride.Plan(_native.OP_ACCUMULATION, site.words, element_bytes=np.dtype(dtype).itemsize,
+                       coefficient_records=selected)
+    values = [cuda(v) for v in (np.array(1.0, real), np.array([2.0], real), np.array([0.5, -1.0, 3.0], real),
+                                np.array(2, np.int32))]
+    outs = [zeros(), zeros()]
+    for side in (0, 1):
+        site.call(side, lambda table: [x, table, *values], [outs[side], scratch_for(site, side, 3, plan.scratch_elements)])
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    site.close()
+
+
+def _device_ms(call, repeats):
+    torch = _torch()
+    call()
+    call()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(repeats):
+        call()
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / repeats
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [np.float32, np.complex64])
+def test_u1_permute_workload_against_the_reference_companion(hosts, companion, dtype):
+    """The U(1) four-leg permute + beta = 1 accumulate at degeneracy scale 40
+    (151 M elements): the permute as an accumulation with unit coefficients,
+    then the update, on both libraries; identical bits, and the device time per
+    call of each (both on the default stream, after two warm-up calls)."""
+    torch = _torch()
+    from tensor0_b200.structure import U1Irrep, degeneracy_structure, hom, space
+    from tensor0_b200.tensor_map import permute_plan
+    v = space(U1Irrep, {q: int(round(40 * np.exp(-q * q / 8))) for q in range(-4, 5)})
+    h = hom((v, v), (v, v))
+    plan = permute_plan(h, (2, 0), (3, 1))
+    n = degeneracy_structure(h).total_dim
+    assert n == plan.output_size == 151162418
+    x = cuda(sample(np.random.default_rng(7), dtype, (1, n)))
+    z = cuda(sample(np.random.default_rng(8), dtype, (1, n)))
+    real = np.float32
+    one = cuda(np.array(1.0, real))
+    item = np.dtype(dtype).itemsize
+    rows = []
+
+    permute = Site(hosts, companion, "accumulation", plan.words, dtype, coefficient_records=[])
+    ours = stride.Plan(_native.OP_ACCUMULATION, permute.words, element_bytes=item, coefficient_records=[])
+    ys = [torch.empty_like(x), torch.empty_like(x)]
+    times = []
+    for side in (0, 1):
+        scratch = scratch_for(permute, side, 1, ours.scratch_elements)
+        times.append(_device_ms(lambda: permute.call(side, lambda table: [x, table], [ys[side], scratch]), 3))
+    assert np.array_equal(bits(ys[0]), bits(ys[1]))
+    rows.append(("permute (accumulation)", 2 * n * item, times))
+    permute.close()
+
+    update = Site(hosts, companion, "update", plan.words, dtype)
+    outs = [torch.empty_like(x), torch.empty_like(x)]
+    times = []
+    for side in (0, 1):
+        times.append(_device_ms(lambda: update.call(side, lambda table: [ys[1], z, one, one, table], [outs[side]]), 3))
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    rows.append(("update (beta = 1)", 3 * n * item, times))
+    update.close()
+
+    for name, nbytes, (reference_ms, our_ms) in rows:
+        print(f"\n{SUFFIX[dtype]} {name}: reference companion {reference_ms:.3f} ms "
+              f"({nbytes / reference_ms / 1e6:.0f} GB/s), this library {our_ms:.3f} ms "
+              f"({nbytes / our_ms / 1e6:.0f} GB/s), ratio {reference_ms / our_ms:.2f}")
