@@ -250,3 +250,37 @@ def test_u1_permute_workload_against_the_reference_companion(hosts, companion, d
         print(f"\n{SUFFIX[dtype]} {name}: reference companion {reference_ms:.3f} ms "
               f"({nbytes / reference_ms / 1e6:.0f} GB/s), this library {our_ms:.3f} ms "
               f"({nbytes / our_ms / 1e6:.0f} GB/s), ratio {reference_ms / our_ms:.2f}")
+
+
+@pytest.mark.gpu
+def test_z2u1_trace_against_the_reference_companion(hosts, companion):
+    """The partial trace of the Z2 x U(1) six-leg tensor (degeneracies 4 / 3,
+    q in -3..3, 548,896,075 f64) over the leg pairs (1, 4) and (2, 5), through
+    both libraries' reduction handlers: within 1e-12 of each other (the
+    summation orders differ), and the time per call of each, taken with CUDA
+    events around five back-to-back calls from this host (Python call frames
+    included for both)."""
+    torch = _torch()
+    from tensor0_b200.structure import ProductSector, U1Irrep, Z2Irrep, degeneracy_structure, hom, space
+    from tensor0_b200.tensor_map import trace_plan
+    w = space(ProductSector(Z2Irrep, U1Irrep), {(p, q): (4, 3)[p] for p in (0, 1) for q in range(-3, 4)})
+    h = hom((w, w, w), (w, w, w))
+    n = degeneracy_structure(h).total_dim
+    tp = trace_plan(h, (1, 2), (4, 5), (0,), (3,))
+    assert n == 548896075 and set(np.asarray(tp.coefficients).tolist()) == {1.0}
+    site = Site(hosts, companion, "reduction", tp.words, np.float64, coefficient_records=[])
+    ours = stride.Plan(_native.OP_REDUCTION, site.words, element_bytes=8, coefficient_records=[])
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(3)
+    x = torch.randn((1, n), generator=gen, device="cuda", dtype=torch.float64)
+    outs = [torch.full((1, ours.output_size), float("nan"), dtype=torch.float64, device="cuda") for _ in (0, 1)]
+    times = []
+    for side in (0, 1):
+        scratch = scratch_for(site, side, 1, ours.scratch_elements)
+        times.append(_device_ms(lambda: site.call(side, lambda table: [x, table], [outs[side], scratch]), 5))
+    expected, got = outs[0].cpu().numpy(), outs[1].cpu().numpy()
+    scale = max(float(np.max(np.abs(expected))), 1e-300)
+    assert float(np.max(np.abs(got - expected))) / scale <= 1e-12
+    site.close()
+    print(f"\nf64 Z2xU1 trace: reference companion {times[0]:.3f} ms, this library {times[1]:.3f} ms per call "
+          f"from this host, ratio {times[0] / times[1]:.1f}")
