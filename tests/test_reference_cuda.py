@@ -14,7 +14,9 @@ Tensor0StrideSumScratchCapacity; this library gets its own packed table.
 CPU: the companion exports the table and packs descriptors.  GPU: on the same
 inputs, this library's copy, update and accumulation handlers reproduce the
 companion's results bit for bit, on random layouts and on the U(1) four-leg
-permute workload, whose device time per call is printed for both.
+permute workload, whose device time per call is printed for both; its dot and
+reduction handlers agree within the precision (their summation orders differ),
+the reduction on the Z2 x U(1) partial trace, timed for both too.
 """
 
 import ctypes
@@ -48,6 +50,8 @@ def companion():
         function = getattr(lib, name)
         function.argtypes = [ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, _RECEIVE]
         function.restype = None
+    lib.Tensor0StrideDotScratchCapacity.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, _RECEIVE]
+    lib.Tensor0StrideDotScratchCapacity.restype = None
     return lib
 
 
@@ -68,7 +72,10 @@ def native_words(lib, entry: str, operation: str, words) -> np.ndarray:
 
     callback = _RECEIVE(receive)
     words = np.ascontiguousarray(words, np.int64)
-    getattr(lib, entry)(OPERATIONS[operation], words.ctypes.data, len(words), None, callback)
+    if entry == "Tensor0StrideDotScratchCapacity":   # the one entry without an operation code
+        lib.Tensor0StrideDotScratchCapacity(words.ctypes.data, len(words), None, callback)
+    else:
+        getattr(lib, entry)(OPERATIONS[operation], words.ctypes.data, len(words), None, callback)
     if result.get("status") != 0:
         raise ValueError(result.get("message", "no result"))
     return result["words"]
@@ -118,18 +125,20 @@ def sample(rng, dtype, shape):
 class Site:
     """One call site on both libraries: instantiate, execute, destroy."""
 
-    def __init__(self, hosts, companion, operation, words, dtype, coefficient_records=None):
+    def __init__(self, hosts, companion, operation, words, dtype, coefficient_records=None, **attrs):
         self.reference, self.ours = hosts
         self.operation, self.dtype = operation, dtype
         self.words = native_words(companion, "Tensor0StridePrepareLayout", operation, words)
-        attrs = {} if coefficient_records is None else {"coefficient_records": list(coefficient_records)}
+        if coefficient_records is not None:
+            attrs["coefficient_records"] = list(coefficient_records)
         self.contexts = (self.reference.instantiate(operation, layout=list(self.words), **attrs),
                          self.ours.instantiate(operation, layout=list(self.words), **attrs))
         self.tables = (cuda(native_words(companion, "Tensor0StridePackOwnerFiber", operation, self.words)),
                        cuda(xla_ffi.descriptor(operation, self.words, dtype,
                                                coefficient_records=coefficient_records or ())))
-        self.capacity = (int(native_words(companion, "Tensor0StrideSumScratchCapacity", operation, self.words)[0])
-                         if operation == "accumulation" else 0)
+        entry = {"accumulation": "Tensor0StrideSumScratchCapacity", "reduction": "Tensor0StrideSumScratchCapacity",
+                 "dot": "Tensor0StrideDotScratchCapacity"}.get(operation)
+        self.capacity = int(native_words(companion, entry, operation, self.words)[0]) if entry else 0
 
     def call(self, side, args, rets):
         host = (self.reference, self.ours)[side]
@@ -188,6 +197,22 @@ def test_handlers_match_the_reference_companion_bit_for_bit(hosts, companion, dt
         site.call(side, lambda table: [x, table, *values], [outs[side], scratch_for(site, side, 3, plan.scratch_elements)])
     assert np.array_equal(bits(outs[0]), bits(outs[1]))
     site.close()
+
+    # Dot (inner / norm): the summation orders differ, so within the precision.
+    records = [stride.AffineRecord((30, 7), (7, 1), 0, (1, 30), 5), stride.AffineRecord((50,), (-2,), 400, (3,), 300)]
+    words = stride.encode_layout(records, source_size=500, output_size=500)
+    a, b = cuda(sample(rng, dtype, (4, 500))), cuda(sample(rng, dtype, (4, 500)))
+    tolerance = 1e-6 if real == np.float32 else 1e-12
+    for conjugate in (0, 1):
+        site = Site(hosts, companion, "dot", words, dtype, conjugate_left=conjugate)
+        plan = stride.Plan(_native.OP_DOT, site.words, element_bytes=np.dtype(dtype).itemsize)
+        outs = [torch.zeros(4, dtype=_torch_dtype(dtype), device="cuda") for _ in (0, 1)]
+        for side in (0, 1):
+            site.call(side, lambda table: [a, b, table], [outs[side], scratch_for(site, side, 4, plan.scratch_elements)])
+        expected, got = outs[0].cpu().numpy(), outs[1].cpu().numpy()
+        magnitude = (a.abs() * b.abs()).sum(dim=1).cpu().numpy()
+        assert np.all(np.abs(got - expected) <= tolerance * magnitude)
+        site.close()
 
 
 def _device_ms(call, repeats):
