@@ -683,7 +683,9 @@ Plan BuildPlan(int32_t operation, const int64_t* words, std::size_t word_count,
   for (std::size_t i = 0; i < coefficient_count; ++i) {
     const int64_t record = coefficient_records[i];
     if (record <= previous || record < 0 || static_cast<uint64_t>(record) >= layout.records.size()) {
-      throw InvalidArgument("coefficient record indices must be increasing and in range");
+      // The reference handlers' wording (accumulation.cu:64, reduction.cu:75).
+      throw InvalidArgument(std::string("CUDA ") + (operation == 4 ? "reduction" : "accumulation") +
+                            " coefficient records must be increasing valid record indices");
     }
     previous = record;
     slot[record] = static_cast<int64_t>(i);

@@ -11,7 +11,9 @@ operand its packed owner/fiber words (Tensor0StridePackOwnerFiber,
 descriptor.cc:407-440), its accumulation scratch sized by
 Tensor0StrideSumScratchCapacity; this library gets its own packed table.
 
-CPU: the companion exports the table and packs descriptors.  GPU: on the same
+CPU: the companion exports the table and packs descriptors, and both
+libraries' instantiate handlers reject the same malformed call sites with the
+same error code and message.  GPU: on the same
 inputs, this library's copy, update and accumulation handlers reproduce the
 companion's results bit for bit, on random layouts and on the U(1) four-leg
 permute workload, whose device time per call is printed for both; its dot and
@@ -25,9 +27,9 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from random_layouts import random_layout
+from random_layouts import random_layout, random_reduction_layout
 from tensor0_b200 import _native, build, stride, xla_ffi
-from xla_host import Host
+from xla_host import HandlerError, Host
 
 LIBRARY = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libt0ref_cuda.so"
 if not LIBRARY.is_file():
@@ -97,6 +99,56 @@ def test_companion_packs_and_rejects_layouts(companion):
     assert capacity.shape == (1,) and capacity[0] >= 0
     with pytest.raises(ValueError):
         native_words(companion, "Tensor0StridePackOwnerFiber", "copy", prepared[:-1])
+
+
+def _instantiate_error(host, operation, attrs):
+    try:
+        ctx = host.instantiate(operation, **attrs)
+    except HandlerError as error:
+        message = error.message
+        for prefix in ("tensor0-native: ", "tensor0-b200: "):
+            message = message.removeprefix(prefix)
+        return error.code, message
+    host.destroy(operation, ctx)
+    return None
+
+
+def test_instantiate_errors_match_the_companion(hosts):
+    """Malformed call sites fail in both libraries' instantiate handlers (host
+    code only) with the same XLA error code and the same message after each
+    library's name prefix; what the companion accepts, this library accepts."""
+    rng = np.random.default_rng(3)
+    words = list(stride.encode_layout(random_layout(rng, 600, 800, 12), source_size=600, output_size=800))
+    reduction, shapes, roles, size = random_reduction_layout(np.random.default_rng(5), 400, 6)
+    reduction_words = list(stride.encode_reduction_layout(reduction, output_shapes=shapes, reduction_axes=roles,
+                                                          source_size=400, output_size=size))
+    cases = [
+        ("copy", {"layout": words[:-1]}),
+        ("copy", {"layout": []}),
+        ("copy", {"layouts": words}),
+        ("update", {"layout": words[:3]}),
+        ("dot", {"layout": words, "conjugate_left": 2}),
+        ("accumulation", {"layout": words, "coefficient_records": [0, 99]}),
+        ("accumulation", {"layout": words, "coefficient_records": [3, 3]}),
+        ("accumulation", {"layout": words, "coefficient_records": [-1]}),
+        ("reduction", {"layout": reduction_words, "coefficient_records": [len(reduction)]}),
+        ("reduction", {"layout": reduction_words[:-2], "coefficient_records": []}),
+    ]
+    # Raw words {version, source size, output size, records, then per record
+    # rank, source offset, output offset, shape, source strides, output strides}.
+    record = [2, 0, 0, 3, 4, 4, 1, 1, 3]
+    cases += [(operation, {"layout": layout}) for operation in ("copy", "update") for layout in (
+        [1, 11, 12, 1, *record],                         # source out of bounds
+        [1, 12, 11, 1, *record],                         # output out of bounds
+        [1, 12, 12, 2, *record, 1, 0, 0, 2, 1, 1],       # two records write output 0 and 1: accepted by both
+        [1, 12, 12, 1, 2, 0, 0, -3, 4, 4, 1, 1, 3],      # negative extent
+        [2, 12, 12, 1, *record],                         # unknown version
+        [1, 12, 12, 2, *record],                         # fewer records than announced
+    )]
+    reference, ours = hosts
+    for operation, attrs in cases:
+        expected = _instantiate_error(reference, operation, attrs)
+        assert _instantiate_error(ours, operation, attrs) == expected, (operation, attrs, expected)
 
 
 # ---------------------------------------------------------------------------
