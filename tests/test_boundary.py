@@ -78,9 +78,9 @@ def test_accumulation_allows_zero_stride_fibers_but_not_collisions(lib):
 
 def test_coefficient_records_must_increase(lib):
     words = [1, 4, 4, 2, 1, 0, 0, 2, 1, 1, 1, 2, 2, 2, 1, 1]
-    assert "coefficient record indices must be increasing" in plan_error(_native.OP_ACCUMULATION, words,
-                                                                         records=[1, 0])
-    assert "coefficient record indices" in plan_error(_native.OP_ACCUMULATION, words, records=[2])
+    message = plan_error(_native.OP_ACCUMULATION, words, records=[1, 0])
+    assert "CUDA accumulation coefficient records must be increasing valid record indices" in message
+    assert "valid record indices" in plan_error(_native.OP_ACCUMULATION, words, records=[2])
 
 
 def test_reduction_validation(lib):
