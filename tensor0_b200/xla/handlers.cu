@@ -402,7 +402,7 @@ ffi::Error Update(UpdateState* state, ffi::AnyBuffer source, ffi::BufferR2<Dtype
     if (source.element_type() != Dtype) {
       throw std::invalid_argument("CUDA update supports only same-dtype F32/F64/C64/C128 storage");
     }
-    if (source.dimensions().size() != 2) throw std::invalid_argument("CUDA update source must be rank-two");
+    if (source.dimensions().size() != 2) throw std::invalid_argument("CUDA update source storage must be rank-two");
     const int dtype = StorageDtype(Dtype);
     const Engine engine = PlanFor(state, dtype, descriptor, "update");
     t0b_plan_info info{};

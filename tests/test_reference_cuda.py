@@ -151,6 +151,55 @@ def test_instantiate_errors_match_the_companion(hosts):
         assert _instantiate_error(ours, operation, attrs) == expected, (operation, attrs, expected)
 
 
+def test_execute_validation_matches_the_companion(hosts, companion):
+    """Execute frames that fail the host-side checks (buffer ranks, dimensions,
+    dtypes, descriptor length, coefficient operands) fail in both libraries
+    with the same error code and message; the addresses are never
+    dereferenced, so no device is needed."""
+    from xla_host import F32, F64, S32, S64
+    records = random_layout(np.random.default_rng(3), 600, 800, 12)
+    raw = stride.encode_layout(records, source_size=600, output_size=800)
+    reference, ours = hosts
+    for operation, attrs in (("copy", {}), ("update", {}), ("accumulation", {"coefficient_records": [1]})):
+        words = native_words(companion, "Tensor0StridePrepareLayout", operation, raw)
+        lengths = (len(native_words(companion, "Tensor0StridePackOwnerFiber", operation, words)),
+                   len(xla_ffi.descriptor(operation, words, np.float64, **attrs)))
+        capacity = scratch_elements = 0
+        if operation == "accumulation":
+            capacity = int(native_words(companion, "Tensor0StrideSumScratchCapacity", operation, words)[0])
+            scratch_elements = stride.Plan(_native.OP_ACCUMULATION, words, element_bytes=8,
+                                           coefficient_records=[1]).scratch_elements
+
+        def frame(side, x=(2, 600), out=(2, 800), x_dtype=F64, extra_words=0, coefficients=((F64, (2,)),)):
+            # Every buffer at its own address, 1 GiB apart, so that no overlap check fires.
+            address = iter(range(1 << 30, 1 << 40, 1 << 30))
+            table = (S64, next(address), (lengths[side] + extra_words,))
+            source, result = (x_dtype, next(address), x), (F64, next(address), out)
+            if operation == "copy":
+                return [source, table], [result]
+            if operation == "update":
+                return [source, (F64, next(address), out), (F64, next(address), ()), (F64, next(address), (2,)),
+                        table], [result]
+            scratch = (F64, next(address), (out[0], (capacity, scratch_elements)[side]))
+            return [source, table, *[(c, next(address), d) for c, d in coefficients]], [result, scratch]
+
+        cases = [dict(x=(2, 601)), dict(out=(2, 801)), dict(x=(3, 600)), dict(x=(600,)), dict(x_dtype=F32),
+                 dict(extra_words=1)]
+        if operation == "accumulation":
+            cases += [dict(coefficients=()), dict(coefficients=((F64, (3,)),)), dict(coefficients=((S64, ()),)),
+                      dict(coefficients=((S32, ()), (S32, ())))]
+        for case in cases:
+            results = []
+            for side, host in enumerate(hosts):
+                ctx = host.instantiate(operation, layout=list(words), **attrs)
+                args, rets = frame(side, **case)
+                with pytest.raises(HandlerError) as error:
+                    host.execute(operation, "f64", ctx, args, rets)
+                host.destroy(operation, ctx)
+                results.append((error.value.code, error.value.message.removeprefix("tensor0-native: ")))
+            assert results[0] == results[1], (operation, case, results)
+
+
 # ---------------------------------------------------------------------------
 # GPU: this library against the companion on the same inputs.
 
