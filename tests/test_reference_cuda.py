@@ -200,6 +200,51 @@ def test_execute_validation_matches_the_companion(hosts, companion):
             assert results[0] == results[1], (operation, case, results)
 
 
+def test_reduction_and_dot_execute_validation_matches_the_companion(hosts, companion):
+    """The same comparison for the reduction and dot handlers."""
+    from xla_host import F32, F64, S64
+    reduction, shapes, roles, size = random_reduction_layout(np.random.default_rng(5), 400, 6)
+    reduction_raw = stride.encode_reduction_layout(reduction, output_shapes=shapes, reduction_axes=roles,
+                                                   source_size=400, output_size=size)
+    dot_raw = stride.encode_layout([stride.AffineRecord((30, 7), (7, 1), 0, (1, 30), 5)], source_size=500,
+                                   output_size=500)
+    for operation, raw, n_in, n_out in (("reduction", reduction_raw, 400, size), ("dot", dot_raw, 500, None)):
+        words = native_words(companion, "Tensor0StridePrepareLayout", operation, raw)
+        entry = "Tensor0StrideSumScratchCapacity" if operation == "reduction" else "Tensor0StrideDotScratchCapacity"
+        capacity = int(native_words(companion, entry, operation, words)[0])
+        plan = stride.Plan(_native.OP_REDUCTION if operation == "reduction" else _native.OP_DOT, words,
+                           element_bytes=8)
+        lengths = (len(native_words(companion, "Tensor0StridePackOwnerFiber", operation, words)),
+                   len(xla_ffi.descriptor(operation, words, np.float64)))
+
+        def frame(side, x=(2, n_in), out=None, dtype=F64, extra_words=0, batches=2):
+            address = iter(range(1 << 30, 1 << 40, 1 << 30))
+            table = (S64, next(address), (lengths[side] + extra_words,))
+            scratch = (F64, next(address), (batches, (capacity, plan.scratch_elements)[side]))
+            if operation == "reduction":
+                result = (F64, next(address), out or (2, n_out))
+                return [(dtype, next(address), x), table], [result, scratch]
+            result = (F64, next(address), out or (2,))
+            return [(dtype, next(address), x), (F64, next(address), (2, n_in)), table], [result, scratch]
+
+        cases = [dict(x=(2, n_in + 1)), dict(x=(3, n_in)), dict(x=(n_in,)), dict(dtype=F32), dict(extra_words=1),
+                 dict(out=(3,) if operation == "dot" else (2, n_out + 1)), dict(batches=3)]
+        for case in cases:
+            results = []
+            for side, host in enumerate(hosts):
+                # The attributes the reference's lowering always passes
+                # (_calls.py:309-327); the companion's dot instantiate does not
+                # survive a missing conjugate_left.
+                extra = {"coefficient_records": []} if operation == "reduction" else {"conjugate_left": 0}
+                ctx = host.instantiate(operation, layout=list(words), **extra)
+                args, rets = frame(side, **case)
+                with pytest.raises(HandlerError) as error:
+                    host.execute(operation, "f64", ctx, args, rets)
+                host.destroy(operation, ctx)
+                results.append((error.value.code, error.value.message.removeprefix("tensor0-native: ")))
+            assert results[0] == results[1], (operation, case, results)
+
+
 # ---------------------------------------------------------------------------
 # GPU: this library against the companion on the same inputs.
 
