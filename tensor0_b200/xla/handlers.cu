@@ -112,21 +112,33 @@ const ffi::TypeInfo kDotTypeInfo = ffi::MakeTypeInfo<DotState>();
 const ffi::TypeInfo kAccumulationTypeInfo = ffi::MakeTypeInfo<AccumulationState>();
 const ffi::TypeInfo kReductionTypeInfo = ffi::MakeTypeInfo<ReductionState>();
 
-// Validate the words once at instantiation with a plan for 8-byte elements.
+// Validate the words once at instantiation with a plan for 8-byte elements,
+// before any prepared state exists: a rejected call site creates none, as in
+// the reference (copy.cu:130-152).
 template <typename S>
 ffi::ErrorOr<std::unique_ptr<S>> Instantiate(int32_t operation, ffi::Span<const int64_t> layout,
                                               ffi::Span<const int64_t> records, uint32_t flags,
                                               int64_t conjugate_left) {
-  auto state = std::make_unique<S>();
-  state->operation = operation;
-  state->words.assign(layout.begin(), layout.end());
-  state->records.assign(records.begin(), records.end());
-  state->flags = flags;
-  state->conjugate_left = conjugate_left;
+  std::vector<int64_t> words(layout.begin(), layout.end());
+  std::vector<int64_t> selected(records.begin(), records.end());
   char error[512] = {0};
   t0b_plan* plan = nullptr;
-  const int status = state->Plan(8, &plan, error, sizeof error);
+  const int status = t0b_plan_create(operation, words.data(), words.size(), selected.data(), selected.size(), 8,
+                                     flags, &plan, error, sizeof error);
   if (status != 0) return ffi::Unexpected(Failure(status, error));
+  std::unique_ptr<S> state;
+  try {
+    state = std::make_unique<S>();
+  } catch (...) {
+    t0b_plan_destroy(plan);
+    throw;
+  }
+  state->operation = operation;
+  state->words = std::move(words);
+  state->records = std::move(selected);
+  state->flags = flags;
+  state->conjugate_left = conjugate_left;
+  state->plans[1] = plan;   // the 8-byte plan
   return std::move(state);
 }
 

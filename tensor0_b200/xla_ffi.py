@@ -101,9 +101,10 @@ def registration_of(lib: ctypes.CDLL) -> dict[str, int]:
     return table
 
 
-def prepared_counts(operation: str) -> tuple[int, int]:
-    """(created, destroyed) prepared states of one operation (copy.cu:130-152)."""
-    lib = library()
+def prepared_counts(operation: str, lib: ctypes.CDLL | None = None) -> tuple[int, int]:
+    """(created, destroyed) prepared states of one operation (copy.cu:130-152),
+    of this library or of another that exports the table."""
+    lib = lib or library()
     stem = "Tensor0StrideCuda" + _capitalized(operation) + "Prepared"
     return int(getattr(lib, stem + "CreatedCount")()), int(getattr(lib, stem + "DestroyedCount")())
 

@@ -151,6 +151,34 @@ def test_instantiate_errors_match_the_companion(hosts):
         assert _instantiate_error(ours, operation, attrs) == expected, (operation, attrs, expected)
 
 
+def test_prepared_state_counts_move_alike(hosts, companion):
+    """Per operation, an instantiate creates one prepared state and its
+    teardown destroys it, in both libraries; a rejected instantiate creates
+    none (copy.cu:130-152)."""
+    records = random_layout(np.random.default_rng(3), 600, 800, 12)
+    words = list(stride.encode_layout(records, source_size=600, output_size=800))
+    reduction, shapes, roles, size = random_reduction_layout(np.random.default_rng(5), 400, 6)
+    reduction_words = list(stride.encode_reduction_layout(reduction, output_shapes=shapes, reduction_axes=roles,
+                                                          source_size=400, output_size=size))
+    sites = {"copy": {"layout": words}, "update": {"layout": words},
+             "dot": {"layout": words, "conjugate_left": 1},
+             "accumulation": {"layout": words, "coefficient_records": [0, 3]},
+             "reduction": {"layout": reduction_words, "coefficient_records": []}}
+    for operation, attrs in sites.items():
+        moves = []
+        for host, lib in zip(hosts, (companion, xla_ffi.library())):
+            before = xla_ffi.prepared_counts(operation, lib)
+            ctx = host.instantiate(operation, **attrs)
+            created = xla_ffi.prepared_counts(operation, lib)
+            host.destroy(operation, ctx)
+            destroyed = xla_ffi.prepared_counts(operation, lib)
+            with pytest.raises(HandlerError):
+                host.instantiate(operation, **{**attrs, "layout": attrs["layout"][:-1]})
+            rejected = xla_ffi.prepared_counts(operation, lib)
+            moves.append([tuple(b - a for a, b in zip(before, after)) for after in (created, destroyed, rejected)])
+        assert moves[0] == moves[1] == [(1, 0), (1, 1), (1, 1)], (operation, moves)
+
+
 def test_execute_validation_matches_the_companion(hosts, companion):
     """Execute frames that fail the host-side checks (buffer ranks, dimensions,
     dtypes, descriptor length, coefficient operands) fail in both libraries
